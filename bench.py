@@ -1,0 +1,427 @@
+#!/usr/bin/env python3
+"""Benchmark: attention forward TFLOP/s (mask-adjusted) on 1..8 B200s.
+
+Workload (per rank, weak scaling): BASELINE config 5 -- causal GQA forward,
+B=1, Hq=64, Hkv=8, N=32768, d=128, bf16 Q/K/V i.i.d. N(0,1) generated on the
+device from a per-rank seed, bf16 O + fp32 LSE.  One step = one forward over
+the rank's inputs (Q 512 MiB + K/V 128 MiB + O 512 MiB, all larger than L2,
+so no flush is needed between steps).  FLOP are mask-adjusted:
+4 * d * (#unmasked (q, k) pairs) per head = 4*128*64*N(N+1)/2 = 1.7593e13.
+
+Ranks share nothing on the data path (heads are independent): the only
+collectives are the barrier and the max-over-ranks of the timed region.
+
+Usage:
+  python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--config c1..c5]
+  torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "dnn-flash_b200"))
+sys.path.insert(0, str(ROOT / "oracle"))
+
+METRIC = "attention fwd TFLOP/s (mask-adjusted)"
+
+# BASELINE.json configs (name -> shape and score_mod)
+CONFIGS = {
+    "c1": dict(B=1, Hq=4, Hkv=4, N=512, D=64, causal=False, alibi=False, softcap=0.0, in_scale=1.0,
+               out="f32", mask=None),
+    "c2": dict(B=4, Hq=16, Hkv=16, N=2048, D=64, causal=True, alibi=False, softcap=0.0, in_scale=1.0,
+               out="f32", mask=None),
+    "c3": dict(B=2, Hq=32, Hkv=32, N=8192, D=128, causal=True, alibi=True, softcap=50.0, in_scale=0.5,
+               out="bf16", mask=None),
+    "c4": dict(B=8, Hq=16, Hkv=16, N=4096, D=128, causal=True, alibi=False, softcap=0.0, in_scale=1.0,
+               out="bf16", mask="window4_prefix4"),
+    "c5": dict(B=1, Hq=64, Hkv=8, N=32768, D=128, causal=True, alibi=False, softcap=0.0, in_scale=1.0,
+               out="bf16", mask=None),
+}
+WORKLOAD_NAMES = {
+    "c1": "c1_mha_noncausal_b1h4_n512_d64",
+    "c2": "c2_mha_causal_b4h16_n2048_d64",
+    "c3": "c3_causal_alibi_softcap50_b2h32_n8192_d128",
+    "c4": "c4_block_sparse_window512_prefix4_b8h16_n4096_d128",
+    "c5": "c5_gqa_causal_hq64_hkv8_n32768_d128",
+}
+
+
+def block_mask_for(cfg):
+    if cfg["mask"] is None:
+        return None
+    import oracle
+
+    return oracle.sliding_window_prefix_mask(cfg["N"] // 128, 4, 4)
+
+
+def flop_per_unit_pairs(cfg):
+    """Mask-adjusted FLOP of one (batch, q-head): 4 * d * #unmasked pairs."""
+    N, D = cfg["N"], cfg["D"]
+    mask = block_mask_for(cfg)
+    if mask is None:
+        pairs = N * (N + 1) // 2 if cfg["causal"] else N * N
+    else:
+        # element-level: allowed block and (causal) kj <= qi
+        pairs = 0
+        nb = mask.shape[0]
+        for qb in range(nb):
+            for kb in range(nb):
+                if not mask[qb, kb]:
+                    continue
+                if cfg["causal"] and kb == qb:
+                    pairs += 128 * 129 // 2
+                elif not cfg["causal"] or kb < qb:
+                    pairs += 128 * 128
+    return 4 * D * pairs
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            d = json.loads(path.read_text())
+            return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), d.get("hbm_gbs", 6650.0), "measured"
+        except (OSError, ValueError):
+            pass
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def profiled_traffic(workload):
+    """DRAM bytes per launch from the committed ncu summary of this kernel/workload, if any."""
+    path = ROOT / "profiles" / f"flash_fwd_{workload.split('_')[0]}.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_reference_sample(cfg, rows, steps, warmup, use_ref=True):
+    """Times the reference's own CPU path on a bounded sample of the workload.
+
+    Sample: every (batch, q-head) of the config restricted to query/key prefix
+    [0, rows) -- for a causal mask the prefix rows are an exact sub-problem.
+    The reference's per-head flash_attention_qk_pv_tile_ws runs on every host
+    core through oracle/_ref's (batch x head) thread pool, with the TensorFlow
+    op's default tiles (query_block_size=16, key_block_size=32).
+    """
+    import numpy as np
+
+    import oracle
+
+    B, Hq, Hkv, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"]
+    rng = np.random.default_rng(7)
+    R = rows
+    q = oracle.round_bf16(rng.standard_normal((B, Hq, R, D)).astype(np.float32) * cfg["in_scale"])
+    k = oracle.round_bf16(rng.standard_normal((B, Hkv, R, D)).astype(np.float32) * cfg["in_scale"])
+    v = oracle.round_bf16(rng.standard_normal((B, Hkv, R, D)).astype(np.float32) * cfg["in_scale"])
+    cores = os.cpu_count() or 1
+    kind = "reference" if (use_ref and oracle.ref_available()) else "port"
+    kw = dict(causal=cfg["causal"], q_block=16, k_block=32, nthreads=cores)
+    if cfg["alibi"]:
+        kw["alibi_slopes"] = oracle.alibi_slopes(Hq)
+    if kind == "reference" and cfg["softcap"] > 0:
+        kind = "port"  # the reference has no soft-cap
+    if kind == "port":
+        kw["softcap"] = cfg["softcap"]
+    sub = dict(cfg, N=R, mask=None)
+    flop = flop_per_unit_pairs(sub) * B * Hq
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        if kind == "reference":
+            oracle.ref_fwd("flash_ws", q, k, v, **kw)
+        else:
+            oracle.flash_fwd(q, k, v, want_lse=False, **kw)
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    t = statistics.mean(times)
+    return {
+        "value": flop / t / 1e12,
+        "unit": "TFLOP/s",
+        "cores": min(cores, B * Hq),
+        "kind": kind,
+        "sample": f"{B}x{Hq} (batch x q-head) units on query/key prefix [0,{R}) of the workload, "
+                  f"{flop / 1e9:.1f} GFLOP per step, tiles 16x32, {kw['nthreads']} threads, mean of {len(times)}",
+        "seconds_per_step": t,
+    }
+
+
+def run_reference_arm(args, cfg, workload):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    rows = args.ref_rows
+    base = cpu_reference_sample(cfg, rows, args.steps, args.warmup)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": base["value"],
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": base["seconds_per_step"] * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": workload, "sample_rows": rows, "note": "CPU reference on host cores"},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, cfg, workload):
+    import numpy as np
+    import torch
+
+    import odf_b200
+
+    world, rank, local = dist_setup()
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    B, Hq, Hkv, N, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["N"], cfg["D"]
+    out_dtype = torch.bfloat16 if cfg["out"] == "bf16" else torch.float32
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    s = cfg["in_scale"]
+    q = (torch.randn((B, Hq, N, D), generator=g, device=dev) * s).to(torch.bfloat16)
+    k = (torch.randn((B, Hkv, N, D), generator=g, device=dev) * s).to(torch.bfloat16)
+    v = (torch.randn((B, Hkv, N, D), generator=g, device=dev) * s).to(torch.bfloat16)
+    o = torch.empty((B, Hq, N, D), dtype=out_dtype, device=dev)
+    lse = torch.empty((B, Hq, N), dtype=torch.float32, device=dev)
+    mask = block_mask_for(cfg)
+    flop_rank = flop_per_unit_pairs(cfg) * B * Hq
+    launches_per_step = 2 if mask is not None else 1
+
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        odf_b200.flash_fwd(q, k, v, causal=cfg["causal"], alibi=cfg["alibi"], softcap=cfg["softcap"],
+                           block_mask=mask, out=o, lse_out=lse)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_begin = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t_begin.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    total_ms = t_begin.elapsed_time(t_end)
+    per_launch_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    status = odf_b200.device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status}: an in-kernel wait timed out")
+
+    # e2e through the host entry (pinned host buffers, H2D + D2H inside the timed region)
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    hq = q.cpu().pin_memory()
+    hk = k.cpu().pin_memory()
+    hv = v.cpu().pin_memory()
+    ho = torch.empty(o.shape, dtype=out_dtype).pin_memory()
+    hl = torch.empty(lse.shape, dtype=torch.float32).pin_memory()
+    hqn, hkn, hvn = (t.view(torch.int16).numpy().view(np.uint16) for t in (hq, hk, hv))
+    hon = ho.view(torch.int16).numpy().view(np.uint16) if out_dtype == torch.bfloat16 else ho.numpy()
+    hln = hl.numpy()
+
+    def e2e_step():
+        odf_b200.flash_fwd_host(hqn, hkn, hvn, causal=cfg["causal"], alibi=cfg["alibi"], softcap=cfg["softcap"],
+                                block_mask=mask, out=hon, lse_out=hln)
+
+    e2e_step()  # warm the host-entry pool
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+    d2h = ho.numel() * ho.element_size() + hl.numel() * 4
+
+    vals = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    total_ms, e2e_s = float(vals[0]), float(vals[1])
+
+    peak, peak_sus, hbm, peak_kind = measured_peaks()
+    value = world * flop_rank * args.steps / (total_ms * 1e-3) / 1e12
+    avg_launch_ms = statistics.mean(per_launch_ms)
+    achieved = flop_rank / (avg_launch_ms * 1e-3) / 1e12
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": workload,
+                "batch_per_gpu": B, "global_batch": B * world, "heads_q": Hq, "heads_kv": Hkv, "seq_len": N,
+                "head_dim": D, "causal": cfg["causal"], "alibi": cfg["alibi"], "softcap": cfg["softcap"],
+                "block_mask": cfg["mask"], "out_dtype": cfg["out"], "lse": True,
+                "parallelism": f"(batch x head) shards, {world} GPU(s), no collective on the data path",
+                "flop_per_gpu_step": flop_rank,
+                "l2": "inputs larger than L2 (Q 512 MiB, K/V 128 MiB, O 512 MiB); no flush needed",
+            },
+            "roofline": {
+                "bound": "tensor",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "peak_kind": f"{peak_kind} bf16 burst (cuBLAS); sustained {peak_sus}",
+                "frac_of_sustained": achieved / peak_sus,
+                "traffic": profiled_traffic(workload),
+                "kernel": "flash_fwd_kernel<128,0>",
+                "avg_launch_ms": avg_launch_ms,
+            },
+            "e2e": {"value": world * flop_rank / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "path": "odf_flash_fwd_host (pinned host buffers)"},
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                base = cpu_reference_sample(cfg, args.cpu_rows, 1, 0)
+                result["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            except Exception as exc:  # the CPU checker is optional for the GPU number
+                result["cpu_baseline"] = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "unavailable",
+                                          "sample": f"{type(exc).__name__}: {exc}"}
+        print(json.dumps(result), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c5")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-rows", type=int, default=3072, help="prefix rows of the CPU baseline sample")
+    ap.add_argument("--ref-rows", type=int, default=1536, help="prefix rows per step of the reference arm")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    workload = WORKLOAD_NAMES[args.config]
+    if args.impl == "reference":
+        return run_reference_arm(args, cfg, workload)
+    return run_ours(args, cfg, workload)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,59 @@
+"""Build step for the sm_100a library (lib/libodf_sm100.so).
+
+Plain nvcc, in-tree, so the shared object travels with the source tree:
+    nvcc -gencode arch=compute_100a,code=sm_100a -O3 -lineinfo -shared ...
+The CUDA runtime is linked statically; the driver API (cuTensorMapEncodeTiled)
+is fetched at run time through cudaGetDriverEntryPoint, so no -lcuda.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+PACKAGE_DIR = Path(__file__).resolve().parent
+ROOT = PACKAGE_DIR.parent
+CSRC = PACKAGE_DIR / "csrc"
+LIB = PACKAGE_DIR / "lib" / "libodf_sm100.so"
+SOURCES = [CSRC / "flash_fwd_sm100.cu", CSRC / "odf_capi.cu"]
+CXX_API_SOURCES = [CSRC / "onednn_flash_api.cpp", CSRC / "planner.cpp"]
+DEPS = SOURCES + CXX_API_SOURCES + [CSRC / "sm100_ptx.cuh", CSRC / "odf_internal.h"] + sorted(
+    (ROOT / "include").rglob("*.h*"))
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC",
+    "-Xlinker", "-Bsymbolic",
+]
+
+
+def nvcc() -> str:
+    cand = os.environ.get("NVCC") or "/usr/local/cuda/bin/nvcc"
+    return cand if Path(cand).exists() else "nvcc"
+
+
+def up_to_date() -> bool:
+    if not LIB.exists():
+        return False
+    t = LIB.stat().st_mtime
+    return all(p.stat().st_mtime <= t for p in DEPS if p.exists())
+
+
+def build_library(force: bool = False, verbose: bool = False) -> Path:
+    if not force and up_to_date():
+        return LIB
+    LIB.parent.mkdir(parents=True, exist_ok=True)
+    srcs = [str(s) for s in SOURCES + CXX_API_SOURCES if s.exists()]
+    cmd = [nvcc(), *NVCC_FLAGS, f"-I{ROOT / 'include'}", f"-I{CSRC}", "-shared", "-o", str(LIB) + ".tmp", *srcs]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    os.replace(str(LIB) + ".tmp", LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    build_library(force="--force" in sys.argv, verbose=True)
+    print(LIB)

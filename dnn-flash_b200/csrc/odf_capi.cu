@@ -1,0 +1,412 @@
+// odf_capi.cu -- the extern "C" boundary (include/odf_sm100.h).
+//
+// Validation mirrors the reference's argument checks
+// (src/onednn_flash/attention.cpp:493-505, batched_attention.cpp:15-21) but
+// reports status codes instead of throwing; the message of the last failure on
+// the calling thread is kept for odf_last_error().
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "odf_internal.h"
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const std::string& msg) {
+    t_last_error = msg;
+    return code;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Fills contiguous [B, H, T, D] strides when all three are zero.
+void resolve_strides(const int64_t in[3], int64_t heads, int64_t tokens, int64_t feat, int64_t out[3]) {
+    if (in[0] == 0 && in[1] == 0 && in[2] == 0) {
+        out[2] = feat;
+        out[1] = tokens * feat;
+        out[0] = heads * tokens * feat;
+    } else {
+        out[0] = in[0];
+        out[1] = in[1];
+        out[2] = in[2];
+    }
+}
+
+struct Resolved {
+    int64_t qs[3], ks[3], vs[3], os[3];
+    int32_t n_qt, n_kt;
+};
+
+// Shared checks of the device and host entries.  `host` relaxes the Q/K/V dtype to F32|BF16.
+int validate(const odf_fwd_params* p, bool host, Resolved* r) {
+    if (p == nullptr) return fail(ODF_ERR_INVALID_ARG, "params must be non-null");
+    if (p->q == nullptr || p->k == nullptr || p->v == nullptr || p->o == nullptr)
+        return fail(ODF_ERR_INVALID_ARG, "attention input/output pointers must be non-null");
+    if (p->batch <= 0 || p->heads_q <= 0 || p->heads_kv <= 0 || p->seqlen_q <= 0 || p->seqlen_k <= 0 ||
+        p->head_dim <= 0 || p->value_dim <= 0)
+        return fail(ODF_ERR_INVALID_ARG, "attention dimensions must be non-zero");
+    if (p->heads_q % p->heads_kv != 0)
+        return fail(ODF_ERR_INVALID_ARG, "heads_q must be a multiple of heads_kv");
+    if (p->head_dim != p->value_dim || (p->head_dim != 64 && p->head_dim != 128))
+        return fail(ODF_ERR_UNSUPPORTED, "the sm_100a kernel supports head_dim == value_dim in {64, 128}");
+    if (host) {
+        if (p->qkv_dtype != ODF_DTYPE_F32 && p->qkv_dtype != ODF_DTYPE_BF16)
+            return fail(ODF_ERR_UNSUPPORTED, "q/k/v dtype must be f32 or bf16");
+    } else if (p->qkv_dtype != ODF_DTYPE_BF16) {
+        return fail(ODF_ERR_UNSUPPORTED, "device q/k/v must be bf16 (convert with odf_convert_f32_to_bf16)");
+    }
+    if (p->o_dtype != ODF_DTYPE_F32 && p->o_dtype != ODF_DTYPE_BF16)
+        return fail(ODF_ERR_UNSUPPORTED, "output dtype must be f32 or bf16");
+    const int64_t n_qt = (p->seqlen_q + odf::kTileQ - 1) / odf::kTileQ;
+    const int64_t n_kt = (p->seqlen_k + odf::kTileK - 1) / odf::kTileK;
+    if (n_qt > 65535 || n_kt > 65535 || p->batch * p->heads_q > 0x7fffffffLL || p->seqlen_q > 0x7fffffffLL ||
+        p->seqlen_k > 0x7fffffffLL)
+        return fail(ODF_ERR_UNSUPPORTED, "sequence length or batch*heads beyond the kernel's grid limits");
+    if (!std::isfinite(p->scale)) return fail(ODF_ERR_INVALID_ARG, "scale must be finite");
+    if (!(p->softcap >= 0.0f) || !std::isfinite(p->softcap))
+        return fail(ODF_ERR_INVALID_ARG, "softcap must be finite and >= 0");
+    if (p->bias_kind != ODF_BIAS_NONE && p->bias_kind != ODF_BIAS_ALIBI)
+        return fail(ODF_ERR_UNSUPPORTED, "only BiasKind::None and BiasKind::AlibiGenerated run on the GPU");
+    if (p->bias_kind == ODF_BIAS_ALIBI && p->alibi_slopes != nullptr && p->heads_q > ODF_MAX_EXPLICIT_SLOPES)
+        return fail(ODF_ERR_UNSUPPORTED, "explicit ALiBi slopes are limited to 256 heads (use generated slopes)");
+    if (p->block_mask != nullptr &&
+        (p->mask_qbs <= 0 || p->mask_kbs <= 0 || p->mask_qblocks <= 0 || p->mask_kblocks <= 0))
+        return fail(ODF_ERR_INVALID_ARG, "BlockMask block sizes and dimensions must be non-zero");
+    resolve_strides(p->q_strides, p->heads_q, p->seqlen_q, p->head_dim, r->qs);
+    resolve_strides(p->k_strides, p->heads_kv, p->seqlen_k, p->head_dim, r->ks);
+    resolve_strides(p->v_strides, p->heads_kv, p->seqlen_k, p->value_dim, r->vs);
+    resolve_strides(p->o_strides, p->heads_q, p->seqlen_q, p->value_dim, r->os);
+    for (int i = 0; i < 3; ++i) {
+        if (r->qs[i] <= 0 || r->ks[i] <= 0 || r->vs[i] <= 0 || r->os[i] <= 0)
+            return fail(ODF_ERR_INVALID_ARG, "strides must be positive (or all zero for contiguous)");
+    }
+    if (host) {
+        const int64_t* all[4] = {p->q_strides, p->k_strides, p->v_strides, p->o_strides};
+        for (auto s : all)
+            if (s[0] || s[1] || s[2]) return fail(ODF_ERR_UNSUPPORTED, "host entry takes contiguous tensors only");
+    } else {
+        if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o))
+            return fail(ODF_ERR_INVALID_ARG, "device pointers must be 16-byte aligned");
+        for (int i = 0; i < 3; ++i) {
+            if (r->qs[i] % 8 || r->ks[i] % 8 || r->vs[i] % 8)
+                return fail(ODF_ERR_INVALID_ARG, "q/k/v strides must be multiples of 8 elements (16 bytes)");
+            if (r->os[i] % (p->o_dtype == ODF_DTYPE_BF16 ? 8 : 4))
+                return fail(ODF_ERR_INVALID_ARG, "output strides must be multiples of 16 bytes");
+        }
+    }
+    r->n_qt = static_cast<int32_t>(n_qt);
+    r->n_kt = static_cast<int32_t>(n_kt);
+    return ODF_OK;
+}
+
+float generated_slope(int64_t h, int64_t heads) {
+    return std::exp2(-8.0f * static_cast<float>(h + 1) / static_cast<float>(heads));
+}
+
+odf::FwdLaunch make_launch(const odf_fwd_params* p, const Resolved& r) {
+    odf::FwdLaunch L;
+    std::memset(&L, 0, sizeof(L));
+    L.q = p->q;
+    L.k = p->k;
+    L.v = p->v;
+    std::copy(r.qs, r.qs + 3, L.q_strides);
+    std::copy(r.ks, r.ks + 3, L.k_strides);
+    std::copy(r.vs, r.vs + 3, L.v_strides);
+    L.head_dim = static_cast<int32_t>(p->head_dim);
+    L.has_alibi = p->bias_kind == ODF_BIAS_ALIBI;
+    L.has_softcap = p->softcap > 0.0f;
+    L.workspace = p->workspace;
+    L.workspace_bytes = p->workspace_bytes;
+    odf::FwdArgs& a = L.args;
+    a.o = p->o;
+    a.lse = p->lse;
+    a.o_stride_b = r.os[0];
+    a.o_stride_h = r.os[1];
+    a.o_stride_t = r.os[2];
+    a.o_bf16 = p->o_dtype == ODF_DTYPE_BF16;
+    a.batch = static_cast<int32_t>(p->batch);
+    a.heads_q = static_cast<int32_t>(p->heads_q);
+    a.heads_kv = static_cast<int32_t>(p->heads_kv);
+    a.m = static_cast<int32_t>(p->seqlen_q);
+    a.n = static_cast<int32_t>(p->seqlen_k);
+    a.n_qt = r.n_qt;
+    a.n_kt = r.n_kt;
+    a.causal = p->causal != 0;
+    a.mode = p->block_mask ? odf::kModeList : (p->causal ? odf::kModeCausal : odf::kModeDense);
+    a.scale = p->scale;
+    a.scale_log2 = p->scale * 1.4426950408889634f;
+    a.softcap = p->softcap;
+    a.inv_softcap = p->softcap > 0.0f ? 1.0f / p->softcap : 0.0f;
+    a.mask = p->block_mask;
+    a.mask_qbs = static_cast<int32_t>(std::min<int64_t>(p->mask_qbs, 0x7fffffff));
+    a.mask_kbs = static_cast<int32_t>(std::min<int64_t>(p->mask_kbs, 0x7fffffff));
+    a.mask_qblocks = static_cast<int32_t>(std::min<int64_t>(p->mask_qblocks, 0x7fffffff));
+    a.mask_kblocks = static_cast<int32_t>(std::min<int64_t>(p->mask_kblocks, 0x7fffffff));
+    a.visits = p->tile_visits;
+    // Generated slopes are evaluated here on the host (for up to 256 heads) so that the
+    // device entry and the chunked host entry use bit-identical values.
+    a.alibi_generated = 0;
+    if (p->bias_kind == ODF_BIAS_ALIBI) {
+        if (p->alibi_slopes != nullptr) {
+            for (int64_t h = 0; h < p->heads_q; ++h) a.alibi_slopes[h] = p->alibi_slopes[h];
+        } else if (p->heads_q <= ODF_MAX_EXPLICIT_SLOPES) {
+            for (int64_t h = 0; h < p->heads_q; ++h) a.alibi_slopes[h] = generated_slope(h, p->heads_q);
+        } else {
+            a.alibi_generated = 1;
+        }
+    }
+    return L;
+}
+
+int run_device(const odf_fwd_params* p, const Resolved& r, cudaStream_t stream) {
+    const size_t need = odf::workspace_bytes_for(p->seqlen_q, p->seqlen_k, p->block_mask != nullptr);
+    if (need > 0 && (p->workspace == nullptr || p->workspace_bytes < need))
+        return fail(ODF_ERR_INVALID_ARG, "a block mask needs a device workspace of odf_fwd_workspace_size() bytes");
+    if (need > 0 && !aligned16(p->workspace)) return fail(ODF_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+    odf::FwdLaunch L = make_launch(p, r);
+    const char* err = "";
+    const int rc = odf::launch_flash_fwd(L, stream, &err);
+    if (rc != ODF_OK) return fail(rc, err);
+    return ODF_OK;
+}
+
+// ------------------------------------------------------------------ host entry
+// Device buffers of the host entry, per thread and device, grown on demand.
+struct HostPool {
+    int device = -1;
+    cudaStream_t streams[2] = {nullptr, nullptr};
+    void* buf[2][8] = {};
+    size_t cap[2][8] = {};
+    void* mask = nullptr;
+    size_t mask_cap = 0;
+    ~HostPool() {
+        // Process teardown may run after the CUDA context is gone; freeing is best-effort.
+        for (auto& set : buf)
+            for (void*& b : set)
+                if (b) cudaFree(b);
+        if (mask) cudaFree(mask);
+        for (auto& s : streams)
+            if (s) cudaStreamDestroy(s);
+    }
+    cudaError_t reserve(int slot, int idx, size_t bytes, void** out) {
+        if (cap[slot][idx] < bytes) {
+            if (buf[slot][idx]) cudaFree(buf[slot][idx]);
+            buf[slot][idx] = nullptr;
+            cap[slot][idx] = 0;
+            cudaError_t e = cudaMalloc(&buf[slot][idx], bytes);
+            if (e != cudaSuccess) return e;
+            cap[slot][idx] = bytes;
+        }
+        *out = buf[slot][idx];
+        return cudaSuccess;
+    }
+};
+thread_local HostPool t_pool;
+
+}  // namespace
+
+extern "C" {
+
+int odf_flash_fwd_sm100(const odf_fwd_params* p, void* stream) {
+    Resolved r;
+    const int rc = validate(p, false, &r);
+    if (rc != ODF_OK) return rc;
+    return run_device(p, r, static_cast<cudaStream_t>(stream));
+}
+
+size_t odf_fwd_workspace_size(const odf_fwd_params* p) {
+    if (p == nullptr) return 0;
+    return odf::workspace_bytes_for(p->seqlen_q, p->seqlen_k, p->block_mask != nullptr);
+}
+
+int odf_flash_fwd_host(const odf_fwd_params* p) {
+    Resolved r;
+    int rc = validate(p, true, &r);
+    if (rc != ODF_OK) return rc;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail(ODF_ERR_NO_DEVICE, "no CUDA device");
+    const char* err = "";
+    rc = odf::ensure_device_ready(device, &err);
+    if (rc != ODF_OK) return fail(rc, err);
+    HostPool& pool = t_pool;
+    if (pool.device != device) {
+        pool.~HostPool();
+        new (&pool) HostPool();
+        pool.device = device;
+    }
+    cudaError_t e = cudaSuccess;
+    for (auto& s : pool.streams)
+        if (!s && e == cudaSuccess) e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+
+    // Work is chunked over (batch, kv-head) units; a unit's Q/O rows (its
+    // heads_q/heads_kv query heads) and K/V rows are contiguous.
+    const int64_t G = p->heads_q / p->heads_kv;
+    const int64_t units = p->batch * p->heads_kv;
+    const int64_t M = p->seqlen_q, N = p->seqlen_k, D = p->head_dim, DV = p->value_dim;
+    const int64_t n_qt = r.n_qt;
+    int64_t n_chunks = std::min<int64_t>(units, 8);
+    while (n_chunks > 1 && (units / n_chunks) * G * n_qt < 2 * 148) --n_chunks;
+    const int64_t per = (units + n_chunks - 1) / n_chunks;
+    const size_t in_es = p->qkv_dtype == ODF_DTYPE_F32 ? 4 : 2;
+    const size_t out_es = p->o_dtype == ODF_DTYPE_F32 ? 4 : 2;
+    const size_t q_unit = static_cast<size_t>(G * M * D), kv_unit = static_cast<size_t>(N * D);
+    const size_t v_unit = static_cast<size_t>(N * DV), o_unit = static_cast<size_t>(G * M * DV);
+
+    const uint8_t* dmask = nullptr;
+    if (p->block_mask) {
+        const size_t mbytes = static_cast<size_t>(p->mask_qblocks * p->mask_kblocks);
+        if (pool.mask_cap < mbytes) {
+            if (pool.mask) cudaFree(pool.mask);
+            pool.mask = nullptr;
+            pool.mask_cap = 0;
+            e = cudaMalloc(&pool.mask, mbytes);
+            if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+            pool.mask_cap = mbytes;
+        }
+        e = cudaMemcpyAsync(pool.mask, p->block_mask, mbytes, cudaMemcpyHostToDevice, pool.streams[0]);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(pool.streams[0]);
+        if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+        dmask = static_cast<const uint8_t*>(pool.mask);
+    }
+    const size_t ws_bytes = odf::workspace_bytes_for(M, N, p->block_mask != nullptr);
+
+    for (int64_t c = 0; c < n_chunks; ++c) {
+        const int64_t u0 = c * per;
+        const int64_t u1 = std::min(units, u0 + per);
+        if (u0 >= u1) break;
+        const int64_t cu = u1 - u0;
+        const int slot = static_cast<int>(c & 1);
+        cudaStream_t st = pool.streams[slot];
+        void *dq, *dk, *dv, *dout, *dlse = nullptr, *dstage = nullptr, *dws = nullptr;
+        if ((e = pool.reserve(slot, 0, cu * q_unit * 2, &dq)) != cudaSuccess ||
+            (e = pool.reserve(slot, 1, cu * kv_unit * 2, &dk)) != cudaSuccess ||
+            (e = pool.reserve(slot, 2, cu * v_unit * 2, &dv)) != cudaSuccess ||
+            (e = pool.reserve(slot, 3, cu * o_unit * out_es, &dout)) != cudaSuccess)
+            return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+        if (p->lse && (e = pool.reserve(slot, 4, cu * G * M * sizeof(float), &dlse)) != cudaSuccess)
+            return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+        if (in_es == 4 &&
+            (e = pool.reserve(slot, 5, cu * std::max(q_unit, std::max(kv_unit, v_unit)) * 4, &dstage)) != cudaSuccess)
+            return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+        if (ws_bytes && (e = pool.reserve(slot, 6, ws_bytes, &dws)) != cudaSuccess)
+            return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+
+        const char* hq = static_cast<const char*>(p->q) + u0 * q_unit * in_es;
+        const char* hk = static_cast<const char*>(p->k) + u0 * kv_unit * in_es;
+        const char* hv = static_cast<const char*>(p->v) + u0 * v_unit * in_es;
+        struct Part { const char* src; void* dst; size_t elems; } parts[3] = {
+            {hq, dq, cu * q_unit}, {hk, dk, cu * kv_unit}, {hv, dv, cu * v_unit}};
+        for (const Part& part : parts) {
+            if (in_es == 2) {
+                e = cudaMemcpyAsync(part.dst, part.src, part.elems * 2, cudaMemcpyHostToDevice, st);
+            } else {
+                e = cudaMemcpyAsync(dstage, part.src, part.elems * 4, cudaMemcpyHostToDevice, st);
+                if (e == cudaSuccess &&
+                    odf::launch_convert_f32_bf16(static_cast<const float*>(dstage), static_cast<uint16_t*>(part.dst),
+                                                 static_cast<int64_t>(part.elems), st) != ODF_OK)
+                    e = cudaErrorLaunchFailure;
+            }
+            if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+        }
+        odf_fwd_params sub = *p;
+        sub.q = dq;
+        sub.k = dk;
+        sub.v = dv;
+        sub.o = dout;
+        sub.lse = static_cast<float*>(dlse);
+        sub.qkv_dtype = ODF_DTYPE_BF16;
+        sub.batch = 1;
+        sub.heads_kv = cu;
+        sub.heads_q = cu * G;
+        sub.block_mask = dmask;
+        sub.workspace = dws;
+        sub.workspace_bytes = ws_bytes;
+        sub.tile_visits = nullptr;
+        // ALiBi slopes are per q-head: shift to this chunk's heads (units never straddle a batch row
+        // of heads when heads are re-based, so slopes are indexed by head within the batch).
+        std::vector<float> slopes;
+        if (p->bias_kind == ODF_BIAS_ALIBI) {
+            slopes.resize(static_cast<size_t>(cu * G));
+            for (int64_t j = 0; j < cu * G; ++j) {
+                const int64_t h = ((u0 * G) + j) % p->heads_q;
+                slopes[j] = p->alibi_slopes ? p->alibi_slopes[h] : generated_slope(h, p->heads_q);
+            }
+            sub.alibi_slopes = slopes.data();
+            if (cu * G > ODF_MAX_EXPLICIT_SLOPES) return fail(ODF_ERR_UNSUPPORTED, "too many heads per chunk for ALiBi");
+        }
+        Resolved rs;
+        rc = validate(&sub, false, &rs);
+        if (rc != ODF_OK) return rc;
+        rc = run_device(&sub, rs, st);
+        if (rc != ODF_OK) return rc;
+        e = cudaMemcpyAsync(static_cast<char*>(p->o) + u0 * o_unit * out_es, dout, cu * o_unit * out_es,
+                            cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess && p->lse)
+            e = cudaMemcpyAsync(p->lse + u0 * G * M, dlse, cu * G * M * sizeof(float), cudaMemcpyDeviceToHost, st);
+        if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+    }
+    for (auto& s : pool.streams) {
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+    }
+    return ODF_OK;
+}
+
+int odf_tile_map_sm100(int64_t seqlen_q, int64_t seqlen_k, int32_t causal, const uint8_t* block_mask,
+                       int64_t mask_qbs, int64_t mask_kbs, int64_t mask_qblocks, int64_t mask_kblocks, uint8_t* out,
+                       void* stream) {
+    if (out == nullptr) return fail(ODF_ERR_INVALID_ARG, "output pointer must be non-null");
+    if (seqlen_q <= 0 || seqlen_k <= 0) return fail(ODF_ERR_INVALID_ARG, "dimensions must be non-zero");
+    if (seqlen_q > 0x7fffffffLL || seqlen_k > 0x7fffffffLL) return fail(ODF_ERR_UNSUPPORTED, "sequence too long");
+    if (block_mask && (mask_qbs <= 0 || mask_kbs <= 0 || mask_qblocks <= 0 || mask_kblocks <= 0))
+        return fail(ODF_ERR_INVALID_ARG, "BlockMask block sizes and dimensions must be non-zero");
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail(ODF_ERR_NO_DEVICE, "no CUDA device");
+    const int rc = odf::launch_tile_map(static_cast<int32_t>(seqlen_q), static_cast<int32_t>(seqlen_k), causal,
+                                        block_mask, static_cast<int32_t>(std::min<int64_t>(mask_qbs, 0x7fffffff)),
+                                        static_cast<int32_t>(std::min<int64_t>(mask_kbs, 0x7fffffff)),
+                                        static_cast<int32_t>(std::min<int64_t>(mask_qblocks, 0x7fffffff)),
+                                        static_cast<int32_t>(std::min<int64_t>(mask_kblocks, 0x7fffffff)), nullptr,
+                                        nullptr, out, static_cast<cudaStream_t>(stream));
+    if (rc != ODF_OK) return fail(rc, "tile map kernel launch failed");
+    return ODF_OK;
+}
+
+int odf_convert_f32_to_bf16(const float* in, uint16_t* out, int64_t count, void* stream) {
+    if ((in == nullptr || out == nullptr) && count > 0) return fail(ODF_ERR_INVALID_ARG, "pointers must be non-null");
+    if (count < 0) return fail(ODF_ERR_INVALID_ARG, "count must be >= 0");
+    const int rc = odf::launch_convert_f32_bf16(in, out, count, static_cast<cudaStream_t>(stream));
+    if (rc != ODF_OK) return fail(rc, "conversion kernel launch failed");
+    return ODF_OK;
+}
+
+int odf_device_status(int32_t* status_out, int32_t clear) {
+    if (status_out == nullptr) return fail(ODF_ERR_INVALID_ARG, "status_out must be non-null");
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail(ODF_ERR_NO_DEVICE, "no CUDA device");
+    const char* err = "";
+    int rc = odf::ensure_device_ready(device, &err);
+    if (rc != ODF_OK) return fail(rc, err);
+    int* ptr = odf::device_status_ptr(device);
+    int value = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&value, ptr, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear) e = cudaMemset(ptr, 0, sizeof(int));
+    if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+    *status_out = value;
+    return ODF_OK;
+}
+
+const char* odf_last_error(void) { return t_last_error.c_str(); }
+
+const char* odf_version(void) { return "dnn-flash-b200 0.1.0 (sm_100a tcgen05/TMA forward)"; }
+
+}  // extern "C"

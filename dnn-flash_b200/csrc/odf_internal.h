@@ -1,0 +1,83 @@
+// odf_internal.h -- launch-side structures shared by the kernel file and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "odf_sm100.h"
+
+namespace odf {
+
+constexpr int kTileQ = ODF_TILE_Q;
+constexpr int kTileK = ODF_TILE_K;
+
+// How the kernel enumerates the KV tiles of a query tile.
+enum TileMode : int32_t {
+    kModeDense = 0,   // every KV tile
+    kModeCausal = 1,  // KV tiles with kt*128 < min(M, (qt+1)*128)
+    kModeList = 2,    // compacted per-query-tile list built from the block mask
+};
+
+// Flags carried in the upper half of a tile-list entry (low 16 bits = kv tile index).
+constexpr uint32_t kListBitmapPartial = 1u << 16;  // some covered mask block is disallowed
+
+// Everything the forward kernel needs besides the three tensor maps.
+struct FwdArgs {
+    void* o;
+    float* lse;
+    int64_t o_stride_b, o_stride_h, o_stride_t;  // elements
+    int32_t o_bf16;
+    int32_t batch, heads_q, heads_kv, m, n;
+    int32_t n_qt, n_kt;
+    int32_t mode;
+    int32_t causal;
+    float scale;        // natural-units softmax scale
+    float scale_log2;   // scale * log2(e)
+    float softcap;      // 0 = off
+    float inv_softcap;
+    const uint8_t* mask;
+    int32_t mask_qbs, mask_kbs, mask_qblocks, mask_kblocks;
+    const uint32_t* tile_list;  // [n_qt, n_kt]
+    const int32_t* tile_count;  // [n_qt]
+    uint8_t* visits;
+    int* status;
+    int32_t alibi_generated;    // slopes = 2^(-8 (h+1) / heads_q)
+    float alibi_slopes[ODF_MAX_EXPLICIT_SLOPES];
+};
+
+// Validated, resolved launch request (device pointers only).
+struct FwdLaunch {
+    const void* q;
+    const void* k;
+    const void* v;
+    int64_t q_strides[3], k_strides[3], v_strides[3];  // elements {b, h, t}
+    int32_t head_dim;
+    int32_t has_alibi;
+    int32_t has_softcap;
+    FwdArgs args;
+    void* workspace;
+    size_t workspace_bytes;
+};
+
+// Launch the tile-list builder (block-mask mode) and the forward kernel on `stream`.
+// Returns ODF_OK or an ODF_ERR_* code; `err` receives a message on failure.
+int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err);
+
+// Tile classification kernel for odf_tile_map_sm100 / the workspace lists.
+int launch_tile_map(int32_t m, int32_t n, int32_t causal, const uint8_t* mask, int32_t mqbs, int32_t mkbs,
+                    int32_t mqblocks, int32_t mkblocks, uint32_t* list, int32_t* count, uint8_t* cls_out,
+                    cudaStream_t stream);
+
+// fp32 -> bf16 conversion kernel.
+int launch_convert_f32_bf16(const float* in, uint16_t* out, int64_t count, cudaStream_t stream);
+
+// Per-device one-time setup (capability check, kernel attributes, status word).
+int ensure_device_ready(int device, const char** err);
+
+// Device address of the status word bounded waits write to (current device).
+int* device_status_ptr(int device);
+
+size_t workspace_bytes_for(int64_t seqlen_q, int64_t seqlen_k, bool has_mask);
+
+}  // namespace odf

@@ -1,0 +1,141 @@
+/*
+ * odf_sm100.h -- C ABI of the B200 (sm_100a) tiled attention forward.
+ *
+ * This is the thin boundary between host code (the C++ API in
+ * include/onednn_flash/, the TensorFlow op, ctypes/cgo/JNI users) and the
+ * CUDA kernels.  Plain pointers, sizes and status codes only; nothing here
+ * throws.  Every entry point replaces one piece of the reference's
+ * hot path, cited beside it.
+ *
+ * Semantics follow the reference's workspace flash path
+ * flash_attention_qk_pv_tile_ws (src/onednn_flash/attention.cpp:486-695):
+ *   s = q.k * scale + bias(qi, kj)          (attention.cpp:619)
+ *   s = softcap * tanh(s / softcap)         (added; no reference counterpart)
+ *   masked (causal kj > qi, top-left aligned, attention.cpp:54-62; BlockMask,
+ *   attention.cpp:70-86) -> -inf, then the online softmax and P.V.
+ * Differences from the reference, by design:
+ *   - Q/K/V are bf16 on the device (the reference is fp32 only); accumulation
+ *     and softmax are fp32.
+ *   - Fully masked rows are written as 0 with LSE = -inf (the reference leaves
+ *     such rows unwritten, attention.cpp:680-682).
+ *   - The per-row log-sum-exp (natural log) is an optional extra output.
+ *   - GQA: heads_q may be a multiple of heads_kv (kv_head = q_head / group).
+ */
+#ifndef ODF_SM100_H
+#define ODF_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (0 = success). */
+#define ODF_OK 0
+#define ODF_ERR_INVALID_ARG 1      /* null pointer, zero/negative size, bad stride, ... */
+#define ODF_ERR_UNSUPPORTED 2      /* shape/dtype/score_mod the sm_100a kernel does not implement */
+#define ODF_ERR_CUDA 3             /* a CUDA runtime/driver call failed */
+#define ODF_ERR_DEVICE_TIMEOUT 4   /* a bounded in-kernel wait gave up (see odf_device_status) */
+#define ODF_ERR_NO_DEVICE 5        /* no sm_100 device current */
+
+/* Element types; values equal onednn_flash::DataType (score_mod_plan.hpp:7-11). */
+#define ODF_DTYPE_F32 0
+#define ODF_DTYPE_BF16 1
+
+/* Bias kinds; values equal onednn_flash::BiasKind (score_mod_plan.hpp:21-28). */
+#define ODF_BIAS_NONE 0
+#define ODF_BIAS_ALIBI 4           /* BiasKind::AlibiGenerated: bias = slope[h] * (kj - qi) */
+
+#define ODF_MAX_EXPLICIT_SLOPES 256
+
+typedef struct odf_fwd_params {
+    /* Tensors.  Device pointers for odf_flash_fwd_sm100, host pointers for
+       odf_flash_fwd_host.  Layout [B, H, T, D] with the element strides below. */
+    const void* q;              /* [B, heads_q,  seqlen_q, head_dim]  */
+    const void* k;              /* [B, heads_kv, seqlen_k, head_dim]  */
+    const void* v;              /* [B, heads_kv, seqlen_k, value_dim] */
+    void* o;                    /* [B, heads_q,  seqlen_q, value_dim] */
+    float* lse;                 /* [B, heads_q, seqlen_q] contiguous, natural log; NULL = not wanted */
+    int32_t qkv_dtype;          /* ODF_DTYPE_BF16 (device); host entry also takes ODF_DTYPE_F32 */
+    int32_t o_dtype;            /* ODF_DTYPE_F32 or ODF_DTYPE_BF16 */
+    int64_t batch, heads_q, heads_kv, seqlen_q, seqlen_k, head_dim, value_dim;
+    /* Element strides {batch, head, token}; all zero = contiguous.  The
+       innermost (feature) stride is always 1. */
+    int64_t q_strides[3], k_strides[3], v_strides[3], o_strides[3];
+    float scale;                /* softmax scale (AttentionOptions::scale) */
+    int32_t causal;             /* AttentionOptions::causal */
+    /* BlockMask (attention.hpp:20-29): u8 row-major [mask_qblocks, mask_kblocks]
+       on the device, non-zero = allowed; NULL = no block mask.  Needs a workspace. */
+    const uint8_t* block_mask;
+    int64_t mask_qbs, mask_kbs, mask_qblocks, mask_kblocks;
+    int32_t bias_kind;          /* ODF_BIAS_NONE or ODF_BIAS_ALIBI */
+    /* ALiBi slopes, HOST array [heads_q] (copied into the launch); NULL with
+       ODF_BIAS_ALIBI = generated slopes 2^(-8 (h+1) / heads_q). */
+    const float* alibi_slopes;
+    float softcap;              /* > 0: s = softcap * tanh(s / softcap); 0 = off */
+    void* workspace;            /* device scratch of odf_fwd_workspace_size() bytes, or NULL if that is 0 */
+    size_t workspace_bytes;
+    /* Optional diagnostics (device, may be NULL): u8 [B*heads_q, q_tiles, kv_tiles],
+       set to 1 for every 128x128 tile the kernel processes (never cleared by it). */
+    uint8_t* tile_visits;
+} odf_fwd_params;
+
+/*
+ * Forward pass on device buffers, asynchronous on `stream` (a cudaStream_t;
+ * NULL = legacy default stream).  Replaces the (batch x head) loop of
+ * flash_attention_batched_qk_pv_tile (src/onednn_flash/batched_attention.cpp:9-49)
+ * and the tile loops of flash_attention_qk_pv_tile_ws (attention.cpp:486-695).
+ */
+int odf_flash_fwd_sm100(const odf_fwd_params* p, void* stream);
+
+/* Device scratch bytes odf_flash_fwd_sm100 needs for these params (0 unless a
+   block mask is given).  Plays the role of AttentionWorkspace::resize
+   (src/onednn_flash/attention_workspace.cpp:5-20). */
+size_t odf_fwd_workspace_size(const odf_fwd_params* p);
+
+/*
+ * Forward pass on HOST buffers (pageable or pinned) through the current
+ * device; blocks until the result is in `p->o` / `p->lse`.  Q/K/V may be
+ * ODF_DTYPE_F32 (converted to bf16 on the device) or ODF_DTYPE_BF16.  Host to
+ * device copies, kernels and device to host copies are pipelined over chunks
+ * of (batch, kv-head).  This is the call the reference's fp32 host API
+ * flash_attention_batched_qk_pv_tile (batched_attention.hpp:26-31) and the
+ * TensorFlow op (tensorflow_ops/onednn_flash_attention_op.cc:126-131) make.
+ * The block mask and ALiBi slopes are host arrays here.
+ */
+int odf_flash_fwd_host(const odf_fwd_params* p);
+
+/*
+ * Tile map of the 128x128 tiling (the skip set): out[qt * kv_tiles + kt] =
+ * 0 skipped, 1 processed with no masked element, 2 processed with an element
+ * mask.  Skipped iff causal and kt*128 >= min(seqlen_q, (qt+1)*128) (the
+ * reference's causal break, attention.cpp:537-539) or every BlockMask block
+ * the tile covers is disallowed.  Device pointers; asynchronous on `stream`.
+ */
+int odf_tile_map_sm100(int64_t seqlen_q, int64_t seqlen_k, int32_t causal, const uint8_t* block_mask,
+                       int64_t mask_qbs, int64_t mask_kbs, int64_t mask_qblocks, int64_t mask_kblocks,
+                       uint8_t* out, void* stream);
+
+/* Convert fp32 -> bf16 (round to nearest even) on the device, asynchronous. */
+int odf_convert_f32_to_bf16(const float* in, uint16_t* out, int64_t count, void* stream);
+
+/* Reads (and, if `clear`, resets) the device-side status word of the current
+   device that bounded in-kernel waits set on timeout.  Synchronises the device. */
+int odf_device_status(int32_t* status_out, int32_t clear);
+
+/* Message for the last non-zero status returned on this host thread. */
+const char* odf_last_error(void);
+
+/* Library version string. */
+const char* odf_version(void);
+
+/* Tile geometry of the kernel (for sizing tile_visits and tile maps). */
+#define ODF_TILE_Q 128
+#define ODF_TILE_K 128
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ODF_SM100_H */

@@ -1,0 +1,88 @@
+"""CPU-only checks of the C ABI library: it loads, exports every symbol the
+headers declare, and its host-side validation rejects bad arguments before any
+CUDA call (no GPU needed for those paths)."""
+from __future__ import annotations
+
+import ctypes as C
+
+import pytest
+
+import odf_b200
+
+
+def test_library_loads_and_reports_version():
+    lib = odf_b200.load_library()
+    assert "sm_100a" in odf_b200.version()
+    assert lib is odf_b200.load_library()
+
+
+def test_every_declared_symbol_is_exported():
+    names = odf_b200.declared_symbols()
+    expected = {"odf_flash_fwd_sm100", "odf_fwd_workspace_size", "odf_flash_fwd_host", "odf_tile_map_sm100",
+                "odf_convert_f32_to_bf16", "odf_device_status", "odf_last_error", "odf_version"}
+    assert expected <= set(names), f"headers lost a declaration: {expected - set(names)}"
+    lib = odf_b200.load_library()
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def _params(**over):
+    p = odf_b200.FwdParams()
+    dummy = 4096  # never dereferenced: validation fails first
+    p.q = p.k = p.v = p.o = dummy
+    p.qkv_dtype, p.o_dtype = odf_b200.ODF_DTYPE_BF16, odf_b200.ODF_DTYPE_F32
+    p.batch, p.heads_q, p.heads_kv, p.seqlen_q, p.seqlen_k, p.head_dim, p.value_dim = 1, 2, 2, 128, 128, 64, 64
+    p.scale = 0.125
+    for k, v in over.items():
+        setattr(p, k, v)
+    return p
+
+
+@pytest.mark.parametrize("field,value,code", [
+    ("q", None, odf_b200.ODF_ERR_INVALID_ARG),
+    ("o", None, odf_b200.ODF_ERR_INVALID_ARG),
+    ("batch", 0, odf_b200.ODF_ERR_INVALID_ARG),
+    ("seqlen_k", 0, odf_b200.ODF_ERR_INVALID_ARG),
+    ("heads_kv", 3, odf_b200.ODF_ERR_INVALID_ARG),
+    ("head_dim", 96, odf_b200.ODF_ERR_UNSUPPORTED),
+    ("value_dim", 128, odf_b200.ODF_ERR_UNSUPPORTED),
+    ("qkv_dtype", odf_b200.ODF_DTYPE_F32, odf_b200.ODF_ERR_UNSUPPORTED),
+    ("o_dtype", 7, odf_b200.ODF_ERR_UNSUPPORTED),
+    ("softcap", -1.0, odf_b200.ODF_ERR_INVALID_ARG),
+    ("scale", float("inf"), odf_b200.ODF_ERR_INVALID_ARG),
+    ("bias_kind", 1, odf_b200.ODF_ERR_UNSUPPORTED),  # BiasKind::SameShapeTile: not on the GPU yet
+    ("seqlen_q", 65536 * 128, odf_b200.ODF_ERR_UNSUPPORTED),
+])
+def test_validation_codes(field, value, code):
+    lib = odf_b200.load_library()
+    rc = lib.odf_flash_fwd_sm100(C.byref(_params(**{field: value})), None)
+    assert rc == code
+    assert odf_b200.last_error()
+
+
+def test_block_mask_needs_sizes_and_workspace():
+    lib = odf_b200.load_library()
+    p = _params(block_mask=4096)
+    assert lib.odf_flash_fwd_sm100(C.byref(p), None) == odf_b200.ODF_ERR_INVALID_ARG
+    p = _params(block_mask=4096, mask_qbs=128, mask_kbs=128, mask_qblocks=1, mask_kblocks=1)
+    assert lib.odf_fwd_workspace_size(C.byref(p)) > 0
+    assert lib.odf_flash_fwd_sm100(C.byref(p), None) == odf_b200.ODF_ERR_INVALID_ARG
+    assert "workspace" in odf_b200.last_error()
+    assert lib.odf_fwd_workspace_size(C.byref(_params())) == 0
+
+
+def test_misaligned_device_pointer_rejected():
+    lib = odf_b200.load_library()
+    assert lib.odf_flash_fwd_sm100(C.byref(_params(q=4096 + 2)), None) == odf_b200.ODF_ERR_INVALID_ARG
+
+
+def test_null_params_and_status_pointer():
+    lib = odf_b200.load_library()
+    assert lib.odf_flash_fwd_sm100(None, None) == odf_b200.ODF_ERR_INVALID_ARG
+    assert lib.odf_device_status(None, 0) == odf_b200.ODF_ERR_INVALID_ARG
+    assert lib.odf_tile_map_sm100(10, 10, 1, None, 0, 0, 0, 0, None, None) == odf_b200.ODF_ERR_INVALID_ARG
+
+
+def test_declared_symbols_parser_sees_all_headers():
+    assert odf_b200.HEADER_PATHS, "include/*.h missing"
+    assert all(n.startswith("odf_") for n in odf_b200.declared_symbols())

@@ -1,0 +1,372 @@
+"""GPU parity: the sm_100a kernel (through the C ABI) against the CPU oracle.
+
+Tolerances (bf16 Q/K/V, fp32 accumulation, compared in fp32):
+  O   relative-L2 <= 1e-2 and max-abs <= 2e-2
+  LSE max-abs    <= 1e-3
+  skipped tile set: bit-exact.
+The oracle restates the reference's flash_attention_qk_pv_tile_ws
+(src/onednn_flash/attention.cpp:486-695); its agreement with the reference
+itself is pinned by tests/test_oracle_vs_reference.py.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from conftest import make_qkv
+
+pytestmark = pytest.mark.gpu
+
+O_REL_L2 = 1e-2
+O_MAX_ABS = 2e-2
+LSE_MAX_ABS = 1e-3
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def to_dev(x, dtype=None):
+    torch = _torch()
+    return torch.from_numpy(np.ascontiguousarray(x)).to("cuda").to(dtype or torch.bfloat16)
+
+
+def run_gpu(q, k, v, **kw):
+    import odf_b200
+
+    torch = _torch()
+    o, lse = odf_b200.flash_fwd(to_dev(q), to_dev(k), to_dev(v), **kw)
+    torch.cuda.synchronize()
+    return o.float().cpu().numpy(), (lse.cpu().numpy() if lse is not None else None)
+
+
+def check_close(o, lse, o_ref, lse_ref, what=""):
+    assert np.all(np.isfinite(o)), f"{what}: non-finite output"
+    diff = o.astype(np.float64) - o_ref.astype(np.float64)
+    denom = max(np.linalg.norm(o_ref.astype(np.float64)), 1e-30)
+    rel = np.linalg.norm(diff) / denom
+    mx = np.abs(diff).max()
+    assert rel <= O_REL_L2, f"{what}: O rel-L2 {rel:.3e}"
+    assert mx <= O_MAX_ABS, f"{what}: O max-abs {mx:.3e}"
+    if lse is not None and lse_ref is not None:
+        fin = np.isfinite(lse_ref)
+        assert np.array_equal(np.isfinite(lse), fin), f"{what}: LSE -inf pattern differs"
+        if fin.any():
+            e = np.abs(lse[fin] - lse_ref[fin]).max()
+            assert e <= LSE_MAX_ABS, f"{what}: LSE max-abs {e:.3e}"
+
+
+def oracle_fwd(q, k, v, **kw):
+    import oracle
+
+    return oracle.flash_fwd(q, k, v, **kw)
+
+
+# --------------------------------------------------------------------------- BASELINE configs
+def test_config1_noncausal_d64():
+    """c1: B1 H4 N512 d64, no mask, fp32 O."""
+    q, k, v = make_qkv(1, 1, 4, 4, 512, 512, 64)
+    o, lse = run_gpu(q, k, v)
+    o_ref, lse_ref = oracle_fwd(q, k, v, q_block=16, k_block=32)
+    check_close(o, lse, o_ref, lse_ref, "c1")
+
+
+def test_config2_causal_d64():
+    """c2: B4 H16 N2048 d64 causal, fp32 O + LSE (full size)."""
+    q, k, v = make_qkv(2, 4, 16, 16, 2048, 2048, 64)
+    o, lse = run_gpu(q, k, v, causal=True)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True)
+    check_close(o, lse, o_ref, lse_ref, "c2")
+
+
+def test_config3_alibi_softcap_reduced():
+    """c3 at reduced length: causal + ALiBi 2^(-8h/H) + soft-cap 50, inputs N(0,1)*0.5, bf16 O."""
+    torch = _torch()
+    import oracle
+
+    H = 8
+    q, k, v = make_qkv(3, 1, H, H, 1024, 1024, 128, scale=0.5)
+    o, lse = run_gpu(q, k, v, causal=True, alibi=True, softcap=50.0, out_dtype=torch.bfloat16)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, alibi_slopes=oracle.alibi_slopes(H), softcap=50.0)
+    check_close(o, lse, o_ref, lse_ref, "c3-reduced")
+
+
+def test_config4_block_sparse_reduced():
+    """c4 at reduced length: 128x128 sliding-window(4 blocks)+prefix(4 blocks) mask with causal."""
+    import oracle
+
+    nb = 12
+    mask = oracle.sliding_window_prefix_mask(nb)
+    q, k, v = make_qkv(4, 2, 2, 2, nb * 128, nb * 128, 128)
+    o, lse = run_gpu(q, k, v, causal=True, block_mask=mask, mask_block=(128, 128))
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, mask=mask, mask_block=(128, 128))
+    check_close(o, lse, o_ref, lse_ref, "c4-reduced")
+
+
+def test_config5_gqa_reduced():
+    """c5 at reduced length: GQA Hq=16, Hkv=2, causal, bf16 O + fp32 LSE."""
+    torch = _torch()
+    q, k, v = make_qkv(5, 1, 16, 2, 1024, 1024, 128)
+    o, lse = run_gpu(q, k, v, causal=True, out_dtype=torch.bfloat16)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True)
+    check_close(o, lse, o_ref, lse_ref, "c5-reduced")
+
+
+# --------------------------------------------------------------------------- edge cases
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("n", [1, 127, 128, 129, 257])
+def test_ragged_lengths(n, causal, d):
+    q, k, v = make_qkv(100 + n, 1, 2, 2, n, n, d)
+    o, lse = run_gpu(q, k, v, causal=causal)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=causal)
+    check_close(o, lse, o_ref, lse_ref, f"n={n} causal={causal} d={d}")
+
+
+@pytest.mark.parametrize("m,n", [(200, 70), (70, 300), (1, 513), (300, 1)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_m_ne_n_top_left_causal(m, n, causal):
+    """M != N: causal stays top-left aligned (kj > qi masked), as attention.cpp:55."""
+    q, k, v = make_qkv(7, 1, 3, 3, m, n, 64)
+    o, lse = run_gpu(q, k, v, causal=causal)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=causal)
+    check_close(o, lse, o_ref, lse_ref, f"m={m} n={n}")
+
+
+def test_fully_masked_rows_zero_and_neg_inf_lse():
+    """A query block with no allowed key block: O rows are 0, LSE is -inf."""
+    mask = np.ones((3, 3), dtype=np.uint8)
+    mask[1, :] = 0
+    q, k, v = make_qkv(8, 1, 2, 2, 300, 300, 64)
+    o, lse = run_gpu(q, k, v, block_mask=mask, mask_block=(128, 128))
+    o_ref, lse_ref = oracle_fwd(q, k, v, mask=mask, mask_block=(128, 128))
+    assert np.all(o[:, :, 128:256] == 0.0)
+    assert np.all(np.isneginf(lse[:, :, 128:256]))
+    check_close(o, lse, o_ref, lse_ref, "masked rows")
+
+
+@pytest.mark.parametrize("mask_block", [(64, 64), (128, 256), (32, 96), (200, 50)])
+def test_block_mask_sizes_independent_of_tiles(mask_block):
+    """BlockMask block sizes need not match the 128x128 tiles (attention.cpp:70-86)."""
+    rng = np.random.default_rng(9)
+    M = N = 520
+    mqb, mkb = -(-M // mask_block[0]), -(-N // mask_block[1])
+    mask = (rng.random((mqb, mkb)) > 0.35).astype(np.uint8)
+    q, k, v = make_qkv(10, 1, 2, 2, M, N, 64)
+    o, lse = run_gpu(q, k, v, causal=True, block_mask=mask, mask_block=mask_block)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, mask=mask, mask_block=mask_block)
+    check_close(o, lse, o_ref, lse_ref, f"mask {mask_block}")
+
+
+def test_block_mask_smaller_than_sequence_disallows_rest():
+    """Blocks outside the bitmap are disallowed (attention.cpp:82-84)."""
+    mask = np.ones((2, 2), dtype=np.uint8)
+    q, k, v = make_qkv(11, 1, 1, 1, 400, 400, 64)
+    o, lse = run_gpu(q, k, v, block_mask=mask, mask_block=(128, 128))
+    o_ref, lse_ref = oracle_fwd(q, k, v, mask=mask, mask_block=(128, 128))
+    check_close(o, lse, o_ref, lse_ref, "short bitmap")
+
+
+@pytest.mark.parametrize("softcap", [0.0, 5.0, 50.0])
+@pytest.mark.parametrize("alibi", [False, True])
+def test_score_mods(alibi, softcap):
+    import oracle
+
+    H = 4
+    q, k, v = make_qkv(12, 2, H, H, 384, 384, 128, scale=1.5)
+    o, lse = run_gpu(q, k, v, causal=True, alibi=alibi, softcap=softcap)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, alibi_slopes=oracle.alibi_slopes(H) if alibi else None,
+                                softcap=softcap)
+    check_close(o, lse, o_ref, lse_ref, f"alibi={alibi} softcap={softcap}")
+
+
+def test_explicit_alibi_slopes_and_noncausal_scale():
+    H = 3
+    slopes = np.array([0.5, 0.03125, 0.25], dtype=np.float32)
+    q, k, v = make_qkv(13, 1, H, H, 260, 300, 64)
+    o, lse = run_gpu(q, k, v, scale=0.3, alibi=True, alibi_slopes=slopes)
+    o_ref, lse_ref = oracle_fwd(q, k, v, scale=0.3, alibi_slopes=slopes)
+    check_close(o, lse, o_ref, lse_ref, "explicit slopes")
+
+
+def test_strided_bmhd_layout_and_bf16_output():
+    """Q/K/V/O given as [B, T, H, D] memory (permuted views), bf16 output."""
+    torch = _torch()
+    import odf_b200
+
+    B, H, M, D = 2, 4, 300, 128
+    q, k, v = make_qkv(14, B, H, H, M, M, D)
+    qd = to_dev(q.transpose(0, 2, 1, 3)).permute(0, 2, 1, 3)
+    kd = to_dev(k.transpose(0, 2, 1, 3)).permute(0, 2, 1, 3)
+    vd = to_dev(v.transpose(0, 2, 1, 3)).permute(0, 2, 1, 3)
+    out = torch.empty((B, M, H, D), dtype=torch.bfloat16, device="cuda").permute(0, 2, 1, 3)
+    o, lse = odf_b200.flash_fwd(qd, kd, vd, causal=True, out=out)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True)
+    check_close(o.float().cpu().numpy(), lse.cpu().numpy(), o_ref, lse_ref, "strided")
+
+
+# --------------------------------------------------------------------------- skip set
+@pytest.mark.parametrize("case", ["causal", "mask", "mask_causal", "ragged"])
+def test_skip_set_bit_exact(case):
+    """The tiles the kernel processes equal the oracle's non-skipped tiles, bit for bit."""
+    torch = _torch()
+    import odf_b200
+    import oracle
+
+    M, N, causal, mask, mb = 1000, 1000, False, None, (128, 128)
+    if case == "causal":
+        causal = True
+    elif case == "mask":
+        mask = oracle.sliding_window_prefix_mask(8)
+    elif case == "mask_causal":
+        causal, mask, mb = True, oracle.sliding_window_prefix_mask(16, 3, 2), (64, 64)
+    else:
+        M, N, causal = 700, 1300, True
+    q, k, v = make_qkv(15, 1, 2, 2, M, N, 64)
+    nqt, nkt = -(-M // 128), -(-N // 128)
+    visits = torch.zeros((2, nqt, nkt), dtype=torch.uint8, device="cuda")
+    odf_b200.flash_fwd(to_dev(q), to_dev(k), to_dev(v), causal=causal, block_mask=mask, mask_block=mb,
+                       visits=visits)
+    torch.cuda.synchronize()
+    ref_map = oracle.tile_map(M, N, 128, 128, causal, mask, mb)
+    dev_map = odf_b200.tile_map(M, N, causal, mask, mb).cpu().numpy()
+    assert np.array_equal(dev_map, ref_map), "device tile map differs from the oracle"
+    processed = visits.cpu().numpy()
+    for h in range(2):
+        assert np.array_equal(processed[h] != 0, ref_map != 0), f"head {h}: processed set differs"
+
+
+def test_config4_full_size_skip_density():
+    """c4 geometry: 32x32 blocks, 228 allowed (22.3%); the kernel visits exactly those tiles."""
+    torch = _torch()
+    import odf_b200
+    import oracle
+
+    mask = oracle.sliding_window_prefix_mask(32)
+    assert int(mask.sum()) == 228
+    ref_map = oracle.tile_map(4096, 4096, 128, 128, True, mask, (128, 128))
+    assert int((ref_map != 0).sum()) == 228
+    dev_map = odf_b200.tile_map(4096, 4096, True, mask, (128, 128)).cpu().numpy()
+    assert np.array_equal(dev_map, ref_map)
+
+
+# --------------------------------------------------------------------------- full-size properties
+def _dense_rows_f64(q, k, v, rows, *, causal, scale, slopes=None, softcap=0.0):
+    """float64 reference for a few query rows of one head (independent numpy restatement)."""
+    qr = q[rows].astype(np.float64)
+    s = qr @ k.astype(np.float64).T * scale
+    kj = np.arange(k.shape[0])[None, :]
+    qi = np.asarray(rows)[:, None]
+    if slopes is not None:
+        s = s + slopes * (kj - qi)
+    if softcap > 0:
+        s = softcap * np.tanh(s / softcap)
+    if causal:
+        s = np.where(kj > qi, -np.inf, s)
+    m = s.max(axis=1, keepdims=True)
+    p = np.exp(s - m)
+    l = p.sum(axis=1, keepdims=True)
+    return (p @ v.astype(np.float64)) / l, (m + np.log(l))[:, 0]
+
+
+def test_config3_full_size_rows():
+    """c3 at full size (B2 H32 N8192 d128, ALiBi + soft-cap 50): sampled rows vs a float64 restatement."""
+    torch = _torch()
+    import odf_b200
+
+    B, H, N, D = 2, 32, 8192, 128
+    g = torch.Generator(device="cuda").manual_seed(33)
+    q = (torch.randn((B, H, N, D), generator=g, device="cuda") * 0.5).to(torch.bfloat16)
+    k = (torch.randn((B, H, N, D), generator=g, device="cuda") * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, H, N, D), generator=g, device="cuda") * 0.5).to(torch.bfloat16)
+    o, lse = odf_b200.flash_fwd(q, k, v, causal=True, alibi=True, softcap=50.0, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.isfinite(o.float()).all() and torch.isfinite(lse).all()
+    slopes = odf_b200.alibi_slopes(H)
+    rows = [0, 1, 127, 128, 4095, 8191]
+    for b, h in [(0, 0), (1, 31), (0, 17)]:
+        qh, kh, vh = (t[b, h].float().cpu().numpy() for t in (q, k, v))
+        o_ref, lse_ref = _dense_rows_f64(qh, kh, vh, rows, causal=True, scale=1 / math.sqrt(D), slopes=slopes[h],
+                                         softcap=50.0)
+        got = o[b, h, rows].float().cpu().numpy()
+        assert np.abs(got - o_ref).max() <= O_MAX_ABS
+        assert np.abs(lse[b, h, rows].cpu().numpy() - lse_ref).max() <= LSE_MAX_ABS
+
+
+def test_config5_full_size_prefix_and_tail():
+    """c5 at full size (Hq64 Hkv8 N32768 d128 causal): prefix rows vs the oracle, tail rows vs float64."""
+    torch = _torch()
+    import odf_b200
+    import oracle
+
+    B, Hq, Hkv, N, D = 1, 64, 8, 32768, 128
+    g = torch.Generator(device="cuda").manual_seed(55)
+    q = torch.randn((B, Hq, N, D), generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn((B, Hkv, N, D), generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn((B, Hkv, N, D), generator=g, device="cuda").to(torch.bfloat16)
+    o, lse = odf_b200.flash_fwd(q, k, v, causal=True, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.isfinite(o.float()).all() and torch.isfinite(lse).all()
+    # causal rows < R only see keys < R: the prefix problem is exact for them
+    R = 640
+    heads = [0, 9, 63]
+    qs = q[:, heads, :R].float().cpu().numpy()
+    ks = k[:, [h // 8 for h in heads], :R].float().cpu().numpy()
+    vs = v[:, [h // 8 for h in heads], :R].float().cpu().numpy()
+    o_ref, lse_ref = oracle.flash_fwd(qs, ks, vs, causal=True)
+    check_close(o[:, heads, :R].float().cpu().numpy(), lse[:, heads, :R].cpu().numpy(), o_ref, lse_ref,
+                "c5 prefix")
+    rows = [N - 129, N - 128, N - 1]
+    for h in (5, 62):
+        qh, kh, vh = q[0, h].float().cpu().numpy(), k[0, h // 8].float().cpu().numpy(), v[0, h // 8].float().cpu().numpy()
+        o64, lse64 = _dense_rows_f64(qh, kh, vh, rows, causal=True, scale=1 / math.sqrt(D))
+        assert np.abs(o[0, h, rows].float().cpu().numpy() - o64).max() <= O_MAX_ABS
+        assert np.abs(lse[0, h, rows].cpu().numpy() - lse64).max() <= LSE_MAX_ABS
+
+
+# --------------------------------------------------------------------------- host entry / status
+@pytest.mark.parametrize("in_dtype", ["f32", "bf16"])
+def test_host_entry_matches_device_entry(in_dtype):
+    """odf_flash_fwd_host (host buffers, fp32 or bf16) equals the device entry on the same values."""
+    import odf_b200
+    import oracle
+
+    H, Hk = 8, 2
+    q, k, v = make_qkv(16, 2, H, Hk, 333, 333, 128)
+    lse = np.empty((2, H, 333), dtype=np.float32)
+    if in_dtype == "f32":
+        hq, hk, hv = q, k, v
+    else:
+        hq, hk, hv = (np.ascontiguousarray((x.view(np.uint32) >> 16).astype(np.uint16)) for x in (q, k, v))
+    o, _ = odf_b200.flash_fwd_host(hq, hk, hv, causal=True, alibi=True, lse_out=lse)
+    o_dev, lse_dev = run_gpu(q, k, v, causal=True, alibi=True)
+    assert np.array_equal(o, o_dev)
+    assert np.array_equal(lse, lse_dev)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, alibi_slopes=oracle.alibi_slopes(H))
+    check_close(o, lse, o_ref, lse_ref, "host entry")
+
+
+def test_invalid_arguments_raise_before_launch():
+    torch = _torch()
+    import odf_b200
+
+    q = torch.zeros((1, 3, 64, 64), dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros((1, 2, 64, 64), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        odf_b200.flash_fwd(q, k, k)  # 3 q-heads over 2 kv-heads
+    q96 = torch.zeros((1, 1, 64, 96), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(odf_b200.OdfError) as e:
+        odf_b200.flash_fwd(q96, q96, q96)
+    assert e.value.code == odf_b200.ODF_ERR_UNSUPPORTED
+
+
+def test_device_status_clean_after_runs():
+    """No bounded in-kernel wait ever gave up during the suite."""
+    import odf_b200
+
+    assert odf_b200.device_status(clear=True) == 0
