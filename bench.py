@@ -415,9 +415,14 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=3072, help="prefix rows of the CPU baseline sample")
     ap.add_argument("--ref-rows", type=int, default=1536, help="prefix rows per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="override N (profiling of a smaller case only; the BASELINE config is the default)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
     workload = WORKLOAD_NAMES[args.config]
+    if args.seq_len is not None:
+        cfg["N"] = args.seq_len
+        workload = f"{workload}_seq{args.seq_len}"
     if args.impl == "reference":
         return run_reference_arm(args, cfg, workload)
     return run_ours(args, cfg, workload)

@@ -1,29 +1,33 @@
 // flash_fwd_sm100.cu -- tiled attention forward for B200 (sm_100a).
 //
-// One CTA computes one 128-row query tile of one (batch, q-head) and walks the
-// KV tiles the tiling does not skip.  It replaces the query-block and key-block
-// loops of the reference's flash_attention_qk_pv_tile_ws
-// (src/onednn_flash/attention.cpp:513-688): the two scalar tile GEMMs
-// (tile_kernel.cpp:57-85) become tcgen05 MMAs with operands staged in shared
-// memory by TMA and accumulators in tensor memory, and the per-row online
-// softmax (attention.cpp:602-674) runs in registers, one thread per query row.
+// One CTA computes a PAIR of 128-row query tiles (Q0, Q1) of one (batch, q-head)
+// and walks the KV tiles the tiling does not skip, loading each K/V tile once for
+// both query tiles.  It replaces the query-block and key-block loops of the
+// reference's flash_attention_qk_pv_tile_ws (src/onednn_flash/attention.cpp:513-688):
+// the scalar tile GEMMs (tile_kernel.cpp:57-85) become tcgen05 MMAs fed by TMA and
+// accumulating in tensor memory, and the per-row online softmax
+// (attention.cpp:602-674) runs in registers, one thread per query row.
 //
-// Warp roles (192 threads):
-//   warps 0-3  softmax + correction + epilogue; thread t owns query row t,
-//              which is TMEM lane t, so row max / row sum need no shuffles.
-//   warp  4    TMA producer: Q once, then K and V of each KV tile into a
-//              STAGES-deep ring.
-//   warp  5    MMA issuer (one thread): S = Q K^T into a double-buffered TMEM
-//              S region, then O += P V once the softmax has published P.
-// The MMA of S(j+1) runs while the softmax works on S(j), and the P V MMA of
-// tile j runs while the softmax computes the exponentials of tile j+1.
-//
-// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).
-// Shared memory (1024-byte aligned 128B-swizzled tiles):
-//   Q [128 x D] | K ring [STAGES][128 x D] | V ring [STAGES][128 x D] | P [128 x 128] | barriers
+// Warp roles (320 threads):
+//   warps 0-3  softmax of Q0 (+ its epilogue); thread t owns row t = TMEM lane t
+//   warps 4-7  softmax of Q1 (+ its epilogue)
+//   warp  8    TMA producer (Q0/Q1 once, then K_j, V_j through a ring of slots);
+//              it also owns the TMEM allocation
+//   warp  9    MMA issuer (one thread)
+// Tensor memory (512 columns):
+//   S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D,256+2D)
+//   P_i (bf16, two per column) is written over the first 64 columns of S_i and is
+//   the A operand of the P.V MMA read straight from tensor memory.
+// MMA issue order per KV tile j (in-order execution on the tensor core):
+//   PV0(j), S0(j+1), PV1(j), S1(j+1)
+// so while the softmax of one query tile runs, the tensor core works on the other
+// tile's P.V and S MMAs.  S_i(j+1) overwrites S_i/P_i only after PV_i(j) was issued.
+// The softmax raises its running max only when a tile's max exceeds it by more than
+// 2^8; the O rescale this needs is done by the softmax thread itself (PV_i(j-1) has
+// completed once S_i(j) has, since a tcgen05 commit tracks all earlier MMAs).
 // Every wait is bounded (2 s); on timeout the CTA records ODF_ERR_DEVICE_TIMEOUT
-// in the device status word, every role leaves its loop, and the TMEM columns
-// are freed before the CTA exits.
+// in the device status word, all roles leave their loops, in-flight copies and
+// MMAs are drained, and the TMEM columns are freed before the CTA exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -39,51 +43,54 @@ namespace odf {
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kWarpProducer = 8;
+constexpr int kWarpMma = 9;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemO = 256;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kChunkBytes = 128 * 128;  // 128 rows x 128 bytes (64 bf16)
-constexpr uint32_t kPBytes = 128 * 128 * 2;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+// The running max is only raised when a tile's max exceeds it by more than this
+// (log2 units), so P stays below 2^8 and O is rescaled rarely.
+constexpr float kRescaleLog2 = 8.0f;
 
 enum ModFlags { kModAlibi = 1, kModSoftcap = 2 };
 
 template <int D>
 struct Config {
-    static constexpr int kStages = (D == 64) ? 3 : 2;
+    static constexpr int kSlots = (D == 64) ? 8 : 4;
     static constexpr int kChunks = D / 64;
-    static constexpr uint32_t kQBytes = 128 * D * 2;
-    static constexpr uint32_t kKVBytes = 128 * D * 2;
-    static constexpr uint32_t kOffK = kQBytes;
-    static constexpr uint32_t kOffV = kOffK + kStages * kKVBytes;
-    static constexpr uint32_t kOffP = kOffV + kStages * kKVBytes;
-    static constexpr uint32_t kOffBar = kOffP + kPBytes;
-    static constexpr int kNumBars = 1 + 3 * kStages + 2 + 2 + 1 + 1 + 1;
+    static constexpr uint32_t kTileBytes = 128 * D * 2;
+    static constexpr uint32_t kOffSlots = 2 * kTileBytes;
+    static constexpr uint32_t kOffBar = kOffSlots + kSlots * kTileBytes;
+    static constexpr int kNumBars = 1 + 2 * kSlots + 2 + 2 + 1 + 1;
     static constexpr uint32_t kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
+    static constexpr uint32_t kTmemO = 256;
 };
 
 struct Bars {
     uint64_t* q_full;
-    uint64_t* k_full;
-    uint64_t* v_full;
-    uint64_t* kv_empty;
-    uint64_t* s_full;
-    uint64_t* s_free;
-    uint64_t* p_full;
-    uint64_t* pv_done;
+    uint64_t* slot_full;
+    uint64_t* slot_empty;
+    uint64_t* s_full;   // [2]
+    uint64_t* p_full;   // [2]
+    uint64_t* mma_done;
     uint64_t* drain;
 };
 
-__device__ __forceinline__ int tile_kt(const FwdArgs& a, int qt, int i, uint32_t* flags) {
-    if (a.mode == kModeList) {
-        const uint32_t e = a.tile_list[static_cast<int64_t>(qt) * a.n_kt + i];
-        *flags = e & 0xFFFF0000u;
-        return static_cast<int>(e & 0xFFFFu);
+// KV tile j of this query-tile pair: kv index in the low 16 bits, kNeed*/kBitmap* flags above.
+__device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, int pair, int j, bool valid1, int qend0, int qend1) {
+    if (a.mode == kModeList) return __ldg(a.tile_list + static_cast<int64_t>(pair) * a.n_kt + j);
+    uint32_t e = static_cast<uint32_t>(j);
+    if (a.mode == kModeCausal) {
+        if (j * kTileK < qend0) e |= kNeed0;
+        if (valid1 && j * kTileK < qend1) e |= kNeed1;
+    } else {
+        e |= kNeed0;
+        if (valid1) e |= kNeed1;
     }
-    *flags = 0;
-    return i;
+    return e;
 }
 
 __device__ __forceinline__ bool mask_allows(const FwdArgs& a, int qi, int kj) {
@@ -105,67 +112,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ FwdArgs args) {
     using Cfg = Config<D>;
-    constexpr int kStages = Cfg::kStages;
+    constexpr int kSlots = Cfg::kSlots;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = ptx::smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-    uint8_t* sQ = smem;
-    uint8_t* sK = smem + Cfg::kOffK;
-    uint8_t* sV = smem + Cfg::kOffV;
-    uint8_t* sP = smem + Cfg::kOffP;
+    uint8_t* sQ = smem;                        // [2][tile]
+    uint8_t* sSlots = smem + Cfg::kOffSlots;   // [kSlots][tile]
     uint64_t* bar_base = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
     Bars bars;
     bars.q_full = bar_base;
-    bars.k_full = bar_base + 1;
-    bars.v_full = bars.k_full + kStages;
-    bars.kv_empty = bars.v_full + kStages;
-    bars.s_full = bars.kv_empty + kStages;
-    bars.s_free = bars.s_full + 2;
-    bars.p_full = bars.s_free + 2;
-    bars.pv_done = bars.p_full + 1;
-    bars.drain = bars.pv_done + 1;
+    bars.slot_full = bar_base + 1;
+    bars.slot_empty = bars.slot_full + kSlots;
+    bars.s_full = bars.slot_empty + kSlots;
+    bars.p_full = bars.s_full + 2;
+    bars.mma_done = bars.p_full + 2;
+    bars.drain = bars.mma_done + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars.drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int bh = blockIdx.x;
-    const int qt = args.n_qt - 1 - static_cast<int>(blockIdx.y);  // longest causal rows first
+    const int pair = args.n_pairs - 1 - static_cast<int>(blockIdx.y);  // longest causal rows first
     const int b = bh / args.heads_q;
     const int h = bh - b * args.heads_q;
     const int hk = h / (args.heads_q / args.heads_kv);
-    const int q0 = qt * kTileQ;
-    const int q_end = min(args.m, q0 + kTileQ);
+    const int q00 = pair * 2 * kTileQ;        // first row of Q0
+    const int q01 = q00 + kTileQ;             // first row of Q1
+    const bool valid1 = q01 < args.m;
+    const int qend0 = min(args.m, q00 + kTileQ);
+    const int qend1 = valid1 ? min(args.m, q01 + kTileQ) : qend0;
 
-    int n_tiles;
+    int n_entries;
     if (args.mode == kModeList) {
-        n_tiles = args.tile_count[qt];
+        n_entries = args.tile_count[pair];
     } else if (args.mode == kModeCausal) {
-        n_tiles = min(args.n_kt, (q_end + kTileK - 1) / kTileK);
+        n_entries = min(args.n_kt, (qend1 + kTileK - 1) / kTileK);
     } else {
-        n_tiles = args.n_kt;
+        n_entries = args.n_kt;
     }
 
     if (threadIdx.x == 0) {
         ptx::mbar_init(bars.q_full, 1);
-        for (int s = 0; s < kStages; ++s) {
-            ptx::mbar_init(&bars.k_full[s], 1);
-            ptx::mbar_init(&bars.v_full[s], 1);
-            ptx::mbar_init(&bars.kv_empty[s], 1);
+        for (int s = 0; s < kSlots; ++s) {
+            ptx::mbar_init(&bars.slot_full[s], 1);
+            ptx::mbar_init(&bars.slot_empty[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
-            ptx::mbar_init(&bars.s_full[s], 1);
-            ptx::mbar_init(&bars.s_free[s], 128);
+        for (int i = 0; i < 2; ++i) {
+            ptx::mbar_init(&bars.s_full[i], 1);
+            ptx::mbar_init(&bars.p_full[i], 128);
         }
-        ptx::mbar_init(bars.p_full, 128);
-        ptx::mbar_init(bars.pv_done, 1);
+        ptx::mbar_init(bars.mma_done, 1);
         ptx::mbar_init(bars.drain, 1);
         *abort_flag = 0;
         ptx::fence_barrier_init();
         ptx::fence_proxy_async_smem();
     }
-    if (warp == 0) {
+    if (warp == kWarpProducer) {
         ptx::tmem_alloc(tmem_slot, kTmemCols);
         ptx::tmem_relinquish();
     }
@@ -174,112 +178,129 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == kWarpProducer) {
         // ------------------------------------------------------------ TMA producer
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0 && n_entries > 0) {
             ptx::prefetch_tmap(&tmQ);
             ptx::prefetch_tmap(&tmK);
             ptx::prefetch_tmap(&tmV);
-            ptx::mbar_arrive_expect_tx(bars.q_full, Cfg::kQBytes);
+            ptx::mbar_arrive_expect_tx(bars.q_full, (valid1 ? 2 : 1) * Cfg::kTileBytes);
             for (int c = 0; c < Cfg::kChunks; ++c) {
-                ptx::tma_load_4d(sQ + c * kChunkBytes, &tmQ, bars.q_full, c * 64, q0, h, b);
+                ptx::tma_load_4d(sQ + c * kChunkBytes, &tmQ, bars.q_full, c * 64, q00, h, b);
             }
-            int issued = 0;
-            for (int i = 0; i < n_tiles; ++i) {
-                const int s = i % kStages;
-                uint32_t fl;
-                const int kt = tile_kt(args, qt, i, &fl);
-                if (i >= kStages) {
-                    if (!ptx::mbar_wait(&bars.kv_empty[s], ((i / kStages) - 1) & 1, abort_flag, args.status,
-                                        ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
+            if (valid1) {
+                for (int c = 0; c < Cfg::kChunks; ++c) {
+                    ptx::tma_load_4d(sQ + Cfg::kTileBytes + c * kChunkBytes, &tmQ, bars.q_full, c * 64, q01, h, b);
+                }
+            }
+            int issued = 0;  // ring uses issued so far (K and V tiles alternate)
+            for (int j = 0; j < n_entries && !*abort_flag; ++j) {
+                const int kt = static_cast<int>(kv_entry(args, pair, j, valid1, qend0, qend1) & 0xFFFFu);
+                for (int half = 0; half < 2; ++half) {
+                    const int t = 2 * j + half;
+                    const int s = t % kSlots;
+                    const int use = t / kSlots;
+                    if (use >= 1 && !ptx::mbar_wait(&bars.slot_empty[s], (use - 1) & 1, abort_flag, args.status,
+                                                    ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
                         break;
+                    uint8_t* dst = sSlots + s * Cfg::kTileBytes;
+                    ptx::mbar_arrive_expect_tx(&bars.slot_full[s], Cfg::kTileBytes);
+                    const void* map = half == 0 ? static_cast<const void*>(&tmK) : static_cast<const void*>(&tmV);
+                    for (int c = 0; c < Cfg::kChunks; ++c) {
+                        ptx::tma_load_4d(dst + c * kChunkBytes, map, &bars.slot_full[s], c * 64, kt * kTileK, hk, b);
+                    }
+                    ++issued;
                 }
-                uint8_t* dk = sK + s * Cfg::kKVBytes;
-                uint8_t* dv = sV + s * Cfg::kKVBytes;
-                ptx::mbar_arrive_expect_tx(&bars.k_full[s], Cfg::kKVBytes);
-                for (int c = 0; c < Cfg::kChunks; ++c) {
-                    ptx::tma_load_4d(dk + c * kChunkBytes, &tmK, &bars.k_full[s], c * 64, kt * kTileK, hk, b);
-                }
-                ptx::mbar_arrive_expect_tx(&bars.v_full[s], Cfg::kKVBytes);
-                for (int c = 0; c < Cfg::kChunks; ++c) {
-                    ptx::tma_load_4d(dv + c * kChunkBytes, &tmV, &bars.v_full[s], c * 64, kt * kTileK, hk, b);
-                }
-                ++issued;
             }
             if (*abort_flag) {
                 // Let copies already issued land before the CTA's shared memory is released.
                 volatile int no_abort = 0;
-                const int first = issued > kStages ? issued - kStages : 0;
-                for (int i = first; i < issued; ++i) {
-                    ptx::mbar_wait(&bars.k_full[i % kStages], (i / kStages) & 1, &no_abort, nullptr, 0, kWaitLimitNs);
-                    ptx::mbar_wait(&bars.v_full[i % kStages], (i / kStages) & 1, &no_abort, nullptr, 0, kWaitLimitNs);
+                const int first = issued > kSlots ? issued - kSlots : 0;
+                for (int t = first; t < issued; ++t) {
+                    ptx::mbar_wait(&bars.slot_full[t % kSlots], (t / kSlots) & 1, &no_abort, nullptr, 0,
+                                   kWaitLimitNs);
                 }
+                ptx::mbar_wait(bars.q_full, 0, &no_abort, nullptr, 0, kWaitLimitNs);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kWarpMma) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0 && n_entries > 0) {
             constexpr uint32_t kIdescQK = ptx::make_idesc_bf16(128, 128, false);
             constexpr uint32_t kIdescPV = ptx::make_idesc_bf16(128, D, true);
-            const uint32_t aQ = ptx::smem_u32(sQ);
-            const uint32_t aK = ptx::smem_u32(sK);
-            const uint32_t aV = ptx::smem_u32(sV);
-            const uint32_t aP = ptx::smem_u32(sP);
+            const uint64_t q_desc0 = ptx::make_sdesc_sw128(ptx::smem_u32(sQ), 16, 1024);
+            const uint64_t q_desc1 = ptx::make_sdesc_sw128(ptx::smem_u32(sQ + Cfg::kTileBytes), 16, 1024);
+            const uint64_t k_desc0 = ptx::make_sdesc_sw128(ptx::smem_u32(sSlots), 16, 1024);
+            const uint64_t v_desc0 = ptx::make_sdesc_sw128(ptx::smem_u32(sSlots), kChunkBytes, 1024);
+            constexpr uint64_t kSlotStep = Cfg::kTileBytes >> 4;  // descriptor units per ring slot
+            int pv_count[2] = {0, 0};
+            bool ok = true;
 
-            auto issue_pv = [&](int j) -> bool {
-                const int s = j % kStages;
-                if (!ptx::mbar_wait(&bars.v_full[s], (j / kStages) & 1, abort_flag, args.status,
-                                    ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
-                    return false;
-                if (!ptx::mbar_wait(bars.p_full, j & 1, abort_flag, args.status, ODF_ERR_DEVICE_TIMEOUT,
-                                    kWaitLimitNs))
-                    return false;
-                ptx::tc_fence_after();
-                const uint32_t vbase = aV + s * Cfg::kKVBytes;
-#pragma unroll
-                for (int kk = 0; kk < kTileK / 16; ++kk) {
-                    const uint64_t pdesc =
-                        ptx::make_sdesc_sw128(aP + (kk >> 2) * kChunkBytes + (kk & 3) * 32, 16, 1024);
-                    const uint64_t vdesc = ptx::make_sdesc_sw128(vbase + kk * 2048, kChunkBytes, 1024);
-                    ptx::mma_bf16_ss(tmem + kTmemO, pdesc, vdesc, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-                }
-                ptx::tc_commit(&bars.kv_empty[s]);
-                ptx::tc_commit(bars.pv_done);
-                return true;
-            };
-
-            bool ok = ptx::mbar_wait(bars.q_full, 0, abort_flag, args.status, ODF_ERR_DEVICE_TIMEOUT,
-                                     kWaitLimitNs);
-            for (int i = 0; ok && i < n_tiles; ++i) {
-                const int s = i % kStages;
-                const int sb = i & 1;
-                if (!ptx::mbar_wait(&bars.k_full[s], (i / kStages) & 1, abort_flag, args.status,
-                                    ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)) {
-                    ok = false;
-                    break;
-                }
-                if (i >= 2 && !ptx::mbar_wait(&bars.s_free[sb], ((i >> 1) - 1) & 1, abort_flag, args.status,
-                                              ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)) {
-                    ok = false;
-                    break;
-                }
-                ptx::tc_fence_after();
-                const uint32_t kbase = aK + s * Cfg::kKVBytes;
+            // S_i = Q_i K^T (SS, M=128, N=128, K=D) into TMEM columns [128 i, 128 i + 128).
+            auto issue_s = [&](int i, int slot) {
+                const uint64_t qd = i == 0 ? q_desc0 : q_desc1;
+                const uint64_t kd = k_desc0 + static_cast<uint64_t>(slot) * kSlotStep;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-                    const uint64_t qdesc = ptx::make_sdesc_sw128(aQ + off, 16, 1024);
-                    const uint64_t kdesc = ptx::make_sdesc_sw128(kbase + off, 16, 1024);
-                    ptx::mma_bf16_ss(tmem + sb * 128, qdesc, kdesc, kIdescQK, kk > 0 ? 1u : 0u);
+                    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4);
+                    ptx::mma_bf16_ss(tmem + i * 128, qd + off, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
                 }
-                ptx::tc_commit(&bars.s_full[sb]);
-                if (i >= 1 && !issue_pv(i - 1)) {
-                    ok = false;
-                    break;
+                ptx::tc_commit(&bars.s_full[i]);
+            };
+            // O_i += P_i V (TS: P_i from TMEM, V MN-major from shared memory; M=128, N=D, K=128).
+            auto issue_pv = [&](int i, int slot) -> bool {
+                if (!ptx::mbar_wait(&bars.p_full[i], pv_count[i] & 1, abort_flag, args.status,
+                                    ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
+                    return false;
+                ptx::tc_fence_after();
+                const uint64_t vd = v_desc0 + static_cast<uint64_t>(slot) * kSlotStep;
+                const uint32_t first = pv_count[i] > 0 ? 1u : 0u;
+#pragma unroll
+                for (int kk = 0; kk < kTileK / 16; ++kk) {
+                    ptx::mma_bf16_ts(tmem + Cfg::kTmemO + i * D, tmem + i * 128 + kk * 8,
+                                     vd + static_cast<uint64_t>(kk * (2048 >> 4)), kIdescPV, (first | kk) ? 1u : 0u);
                 }
+                ++pv_count[i];
+                return true;
+            };
+            auto wait_full = [&](int t) -> bool {
+                return ptx::mbar_wait(&bars.slot_full[t % kSlots], (t / kSlots) & 1, abort_flag, args.status,
+                                      ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+            };
+
+            ok = ptx::mbar_wait(bars.q_full, 0, abort_flag, args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+            uint32_t e = kv_entry(args, pair, 0, valid1, qend0, qend1);
+            if (ok) ok = wait_full(0);
+            if (ok) {
+                ptx::tc_fence_after();
+                if (e & kNeed0) issue_s(0, 0);
+                if (e & kNeed1) issue_s(1, 0);
+                ptx::tc_commit(&bars.slot_empty[0]);
             }
-            if (ok) ok = issue_pv(n_tiles - 1);
-            if (!ok) {
+            for (int j = 0; ok && j < n_entries; ++j) {
+                const int tv = 2 * j + 1;  // V_j ring index
+                const int tk = 2 * j + 2;  // K_{j+1} ring index
+                const bool more = j + 1 < n_entries;
+                const uint32_t en = more ? kv_entry(args, pair, j + 1, valid1, qend0, qend1) : 0u;
+                if (!(ok = wait_full(tv))) break;
+                ptx::tc_fence_after();
+                if ((e & kNeed0) && !(ok = issue_pv(0, tv % kSlots))) break;
+                if (more) {
+                    if (!(ok = wait_full(tk))) break;
+                    ptx::tc_fence_after();
+                    if (en & kNeed0) issue_s(0, tk % kSlots);
+                }
+                if ((e & kNeed1) && !(ok = issue_pv(1, tv % kSlots))) break;
+                ptx::tc_commit(&bars.slot_empty[tv % kSlots]);
+                if (more) {
+                    if (en & kNeed1) issue_s(1, tk % kSlots);
+                    ptx::tc_commit(&bars.slot_empty[tk % kSlots]);
+                }
+                e = en;
+            }
+            if (ok) {
+                ptx::tc_commit(bars.mma_done);
+            } else {
                 // Drain the MMAs already issued before the TMEM columns are freed.
                 volatile int no_abort = 0;
                 ptx::tc_commit(bars.drain);
@@ -287,46 +308,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ------------------------------------------------------------ softmax warps 0-3
-        const int row = threadIdx.x;  // 0..127 == TMEM lane
+        // ------------------------------------------------------------ softmax warps
+        const int qtile = warp >> 2;         // 0: Q0, 1: Q1
+        const int wq = warp & 3;             // TMEM lane quarter
+        const int row = wq * 32 + lane;      // 0..127 == TMEM lane
+        const int q0 = qtile == 0 ? q00 : q01;
         const int qi = q0 + row;
-        const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-        float m_run = -INFINITY;  // running max, log2 units
+        const uint32_t need_bit = qtile == 0 ? kNeed0 : kNeed1;
+        const uint32_t bitmap_bit = qtile == 0 ? kBitmap0 : kBitmap1;
+        const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+        const uint32_t s_addr = tmem + lane_off + qtile * 128;
+        const uint32_t o_addr = tmem + lane_off + Cfg::kTmemO + qtile * D;
+        float m_run = -INFINITY;  // running (reference) max, log2 units
         float l_run = 0.0f;       // running sum relative to m_run
         float slope = 0.0f;
         if (MOD & kModAlibi) {
-            slope = args.alibi_generated ? exp2f(-8.0f * static_cast<float>(h + 1) / static_cast<float>(args.heads_q))
-                                         : args.alibi_slopes[h];
+            slope = args.alibi_generated
+                        ? exp2f(-8.0f * static_cast<float>(h + 1) / static_cast<float>(args.heads_q))
+                        : args.alibi_slopes[h];
         }
         const float slope_log2 = slope * kLog2e;
         bool ok = true;
-        const uint32_t p_row = ptx::smem_u32(sP) + row * 128;
-        const uint32_t swz = static_cast<uint32_t>(row & 7);
+        int cnt = 0;
 
-        for (int i = 0; i < n_tiles; ++i) {
-            uint32_t fl;
-            const int kt = tile_kt(args, qt, i, &fl);
+        for (int j = 0; j < n_entries; ++j) {
+            const uint32_t e = kv_entry(args, pair, j, valid1, qend0, qend1);
+            if (!(e & need_bit)) continue;
+            const int kt = static_cast<int>(e & 0xFFFFu);
             const int k0 = kt * kTileK;
-            const int sb = i & 1;
             // Waits are per thread; the warp re-converges (and agrees) before the
             // .sync.aligned TMEM accesses that follow.
-            const bool got_s = ptx::mbar_wait(&bars.s_full[sb], (i >> 1) & 1, abort_flag, args.status,
-                                              ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
-            if (!__all_sync(0xffffffffu, got_s)) {
+            const bool got = ptx::mbar_wait(&bars.s_full[qtile], cnt & 1, abort_flag, args.status,
+                                            ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+            if (!__all_sync(0xffffffffu, got)) {
                 ok = false;
                 break;
             }
             ptx::tc_fence_after();
             float s[128];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) ptx::tmem_ld32(tmem + lane_off + sb * 128 + c * 32, &s[c * 32]);
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(&bars.s_free[sb]);
+            ptx::tmem_ld128(s_addr, s);
             if (row == 0 && args.visits) {
-                args.visits[(static_cast<int64_t>(bh) * args.n_qt + qt) * args.n_kt + kt] = 1;
+                args.visits[(static_cast<int64_t>(bh) * args.n_qt + (q0 / kTileQ)) * args.n_kt + kt] = 1;
             }
 
-            // score_mod: s*scale (+ ALiBi) (-> soft-cap), in log2 units (attention.cpp:619)
+            // score_mod: s*scale (+ ALiBi) (-> soft-cap), in log2 units (attention.cpp:619).
+            // Without a score_mod the scale is folded into the exponent below (raw scores).
+            const bool raw = (MOD == 0) && (args.scale_log2 > 0.0f);
             if (MOD & kModSoftcap) {
                 const float base = static_cast<float>(k0 - qi);
 #pragma unroll
@@ -342,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 0; c < 128; ++c) {
                     s[c] = fmaf(s[c], args.scale_log2, slope_log2 * (base + static_cast<float>(c)));
                 }
-            } else {
+            } else if (!raw) {
 #pragma unroll
                 for (int c = 0; c < 128; ++c) s[c] *= args.scale_log2;
             }
@@ -350,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // element mask on boundary tiles (attention.cpp:54-62, 608-617)
             const bool ragged = (k0 + kTileK > args.n);
             const bool diag = args.causal && (min(args.n, k0 + kTileK) - 1 > q0);
-            const bool bitmap = (fl & kListBitmapPartial) != 0;
+            const bool bitmap = (e & bitmap_bit) != 0;
             if (ragged || diag || bitmap) {
 #pragma unroll
                 for (int c = 0; c < 128; ++c) {
@@ -362,60 +389,74 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
 
-            // online softmax (attention.cpp:628-644, 662-674)
-            float mx = m_run;
+            // online softmax (attention.cpp:628-644, 662-674) with tree reductions
+            float mx8[8];
 #pragma unroll
-            for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c]);
-            const float m_use = (mx == -INFINITY) ? 0.0f : mx;
-            const float alpha = ptx::ex2(m_run - m_use);
-            float sum = 0.0f;
+            for (int t = 0; t < 8; ++t) mx8[t] = s[t];
 #pragma unroll
-            for (int c = 0; c < 128; ++c) {
-                s[c] = ptx::ex2(s[c] - m_use);
-                sum += s[c];
+            for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+            float tile_max = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            if (raw) tile_max *= args.scale_log2;
+            float alpha = 1.0f;
+            if (m_run == -INFINITY) {
+                m_run = tile_max;  // first valid tile of this row: O holds zeros so far
+            } else if (tile_max > m_run + kRescaleLog2) {
+                alpha = ptx::ex2(m_run - tile_max);
+                m_run = tile_max;
             }
-            l_run = l_run * alpha + sum;
-            m_run = mx;
-
-            if (i > 0) {
-                // P buffer and O are owned by the P V MMA of the previous tile until it completes.
-                const bool got_pv = ptx::mbar_wait(bars.pv_done, (i - 1) & 1, abort_flag, args.status,
-                                                   ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
-                if (!__all_sync(0xffffffffu, got_pv)) {
-                    ok = false;
-                    break;
+            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+            float sum8[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) sum8[t] = 0.0f;
+            // P (bf16 pairs) is packed in place into s[0..63]: element c/2 is written only
+            // after s[c] and s[c+1] were consumed, so no second register array is needed.
+            if (raw) {
+                const float neg = -m_use;
+#pragma unroll
+                for (int c = 0; c < 128; c += 2) {
+                    const float p0 = ptx::ex2(fmaf(s[c], args.scale_log2, neg));
+                    const float p1 = ptx::ex2(fmaf(s[c + 1], args.scale_log2, neg));
+                    sum8[c & 7] += p0;
+                    sum8[(c + 1) & 7] += p1;
+                    s[c >> 1] = __uint_as_float(ptx::pack_bf16x2(p0, p1));
                 }
-                ptx::tc_fence_after();
-            }
-            // P (bf16) into the 128B-swizzled K-major layout the P V MMA reads.
+            } else {
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const uint32_t addr = p_row + (u >> 3) * kChunkBytes + ((((u & 7) ^ swz)) << 4);
-                ptx::st_shared_v4(addr, ptx::pack_bf16x2(s[8 * u + 0], s[8 * u + 1]),
-                                  ptx::pack_bf16x2(s[8 * u + 2], s[8 * u + 3]),
-                                  ptx::pack_bf16x2(s[8 * u + 4], s[8 * u + 5]),
-                                  ptx::pack_bf16x2(s[8 * u + 6], s[8 * u + 7]));
+                for (int c = 0; c < 128; c += 2) {
+                    const float p0 = ptx::ex2(s[c] - m_use);
+                    const float p1 = ptx::ex2(s[c + 1] - m_use);
+                    sum8[c & 7] += p0;
+                    sum8[(c + 1) & 7] += p1;
+                    s[c >> 1] = __uint_as_float(ptx::pack_bf16x2(p0, p1));
+                }
             }
-            // correction: O *= alpha when the running max moved
-            if (i > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+            l_run = l_run * alpha +
+                    (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
+
+            // correction: O_i *= alpha when the reference max moved (PV_i of the previous
+            // tile is complete: the commit that released S_i(j) covers every earlier MMA)
+            if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
                     float o[32];
-                    ptx::tmem_ld32(tmem + lane_off + kTmemO + c * 32, o);
+                    ptx::tmem_ld32(o_addr + c * 32, o);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) o[j] *= alpha;
-                    ptx::tmem_st32(tmem + lane_off + kTmemO + c * 32, o);
+                    for (int t = 0; t < 32; ++t) o[t] *= alpha;
+                    ptx::tmem_st32_nowait(o_addr + c * 32, reinterpret_cast<const uint32_t*>(o));
                 }
             }
-            ptx::fence_proxy_async_smem();
+            // P_i over the first 64 columns of S_i, the A operand of PV_i
+            ptx::tmem_st64_nowait(s_addr, reinterpret_cast<const uint32_t*>(s));
+            ptx::tmem_st_wait();
             ptx::tc_fence_before();
-            ptx::mbar_arrive(bars.p_full);
+            ptx::mbar_arrive(&bars.p_full[qtile]);
+            ++cnt;
         }
 
         // ------------------------------------------------------------ epilogue
-        if (ok && n_tiles > 0) {
-            ok = ptx::mbar_wait(bars.pv_done, (n_tiles - 1) & 1, abort_flag, args.status, ODF_ERR_DEVICE_TIMEOUT,
-                                kWaitLimitNs);
+        if (ok && cnt > 0) {
+            ok = ptx::mbar_wait(bars.mma_done, 0, abort_flag, args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
             ptx::tc_fence_after();
         }
         ok = __all_sync(0xffffffffu, ok);
@@ -427,11 +468,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (int c = 0; c < D / 32; ++c) {
                 float o[32];
-                if (n_tiles > 0) {
-                    ptx::tmem_ld32(tmem + lane_off + kTmemO + c * 32, o);
+                if (cnt > 0) {
+                    ptx::tmem_ld32(o_addr + c * 32, o);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) o[j] = 0.0f;
+                    for (int t = 0; t < 32; ++t) o[t] = 0.0f;
                 }
                 if (valid_row) {
                     if (args.o_bf16) {
@@ -466,62 +507,82 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- teardown
     ptx::tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == kWarpProducer) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, kTmemCols);
     }
 }
 
-// Tile classification / compaction: one warp per query tile, in increasing kv order.
-__global__ void tile_map_kernel(int32_t m, int32_t n, int32_t n_qt, int32_t n_kt, int32_t causal,
-                                const uint8_t* __restrict__ mask, int32_t mqbs, int32_t mkbs, int32_t mqblocks,
-                                int32_t mkblocks, uint32_t* __restrict__ list, int32_t* __restrict__ count,
-                                uint8_t* __restrict__ cls_out) {
-    const int qt = blockIdx.x;
-    const int lane = threadIdx.x;
-    if (qt >= n_qt) return;
+// Classification of one 128x128 tile: 0 skipped, 1 full, 2 element-masked; *bitmap_partial
+// is set when a covered BlockMask block is disallowed (the kernel then tests the bitmap
+// per element).  Skip rule: the reference's causal break (attention.cpp:537-539) or no
+// allowed BlockMask block covered (attention.cpp:70-86).
+__device__ uint32_t classify_tile(int32_t m, int32_t n, int qt, int kt, int32_t causal, const uint8_t* mask,
+                                  int32_t mqbs, int32_t mkbs, int32_t mqblocks, int32_t mkblocks,
+                                  bool* bitmap_partial) {
+    *bitmap_partial = false;
     const int q0 = qt * kTileQ;
     const int q1 = min(m, q0 + kTileQ);
+    const int k0 = kt * kTileK;
+    const int k1 = min(n, k0 + kTileK);
+    if (q0 >= m) return 0;
+    if (causal && k0 >= q1) return 0;
+    uint32_t cls = (causal && k1 - 1 > q0) ? 2u : 1u;
+    if (mask) {
+        bool any_allowed = false, any_denied = false;
+        for (int qb = q0 / mqbs; qb <= (q1 - 1) / mqbs; ++qb) {
+            for (int kb = k0 / mkbs; kb <= (k1 - 1) / mkbs; ++kb) {
+                const bool okb = qb < mqblocks && kb < mkblocks && mask[static_cast<int64_t>(qb) * mkblocks + kb] != 0;
+                any_allowed |= okb;
+                any_denied |= !okb;
+            }
+        }
+        if (!any_allowed) return 0;
+        if (any_denied) {
+            cls = 2;
+            *bitmap_partial = true;
+        }
+    }
+    return cls;
+}
+
+// Per-query-tile classes (odf_tile_map_sm100): one thread per tile.
+__global__ void tile_class_kernel(int32_t m, int32_t n, int32_t n_qt, int32_t n_kt, int32_t causal,
+                                  const uint8_t* __restrict__ mask, int32_t mqbs, int32_t mkbs, int32_t mqblocks,
+                                  int32_t mkblocks, uint8_t* __restrict__ cls_out) {
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<int64_t>(n_qt) * n_kt) return;
+    const int qt = static_cast<int>(idx / n_kt);
+    const int kt = static_cast<int>(idx - static_cast<int64_t>(qt) * n_kt);
+    bool bp;
+    cls_out[idx] = static_cast<uint8_t>(classify_tile(m, n, qt, kt, causal, mask, mqbs, mkbs, mqblocks, mkblocks, &bp));
+}
+
+// Per-pair KV lists (block-mask mode): one warp per query-tile pair, increasing kv order.
+__global__ void pair_list_kernel(int32_t m, int32_t n, int32_t n_pairs, int32_t n_kt, int32_t causal,
+                                 const uint8_t* __restrict__ mask, int32_t mqbs, int32_t mkbs, int32_t mqblocks,
+                                 int32_t mkblocks, uint32_t* __restrict__ list, int32_t* __restrict__ count) {
+    const int pair = blockIdx.x;
+    const int lane = threadIdx.x;
+    if (pair >= n_pairs) return;
     int base = 0;
     for (int kt0 = 0; kt0 < n_kt; kt0 += 32) {
         const int kt = kt0 + lane;
-        uint32_t cls = 0, flags = 0;
+        uint32_t entry = 0;
         if (kt < n_kt) {
-            const int k0 = kt * kTileK;
-            const int k1 = min(n, k0 + kTileK);
-            cls = 1;
-            if (causal && k0 >= q1) {
-                cls = 0;
-            } else {
-                if (causal && k1 - 1 > q0) cls = 2;
-                if (mask) {
-                    bool any_allowed = false, any_denied = false;
-                    for (int qb = q0 / mqbs; qb <= (q1 - 1) / mqbs; ++qb) {
-                        for (int kb = k0 / mkbs; kb <= (k1 - 1) / mkbs; ++kb) {
-                            const bool okb = qb < mqblocks && kb < mkblocks &&
-                                             mask[static_cast<int64_t>(qb) * mkblocks + kb] != 0;
-                            any_allowed |= okb;
-                            any_denied |= !okb;
-                        }
-                    }
-                    if (!any_allowed) {
-                        cls = 0;
-                    } else if (any_denied) {
-                        cls = 2;
-                        flags |= kListBitmapPartial;
-                    }
-                }
+            bool bp0, bp1;
+            const uint32_t c0 = classify_tile(m, n, 2 * pair, kt, causal, mask, mqbs, mkbs, mqblocks, mkblocks, &bp0);
+            const uint32_t c1 = classify_tile(m, n, 2 * pair + 1, kt, causal, mask, mqbs, mkbs, mqblocks, mkblocks, &bp1);
+            if (c0 | c1) {
+                entry = static_cast<uint32_t>(kt) | (c0 ? kNeed0 : 0u) | (c1 ? kNeed1 : 0u) | (bp0 ? kBitmap0 : 0u) |
+                        (bp1 ? kBitmap1 : 0u);
             }
-            if (cls_out) cls_out[static_cast<int64_t>(qt) * n_kt + kt] = static_cast<uint8_t>(cls);
         }
-        const unsigned ballot = __ballot_sync(0xffffffffu, cls != 0);
-        if (cls != 0 && list) {
-            const int pos = base + __popc(ballot & ((1u << lane) - 1u));
-            list[static_cast<int64_t>(qt) * n_kt + pos] = static_cast<uint32_t>(kt) | flags;
-        }
+        const unsigned ballot = __ballot_sync(0xffffffffu, entry != 0);
+        if (entry != 0) list[static_cast<int64_t>(pair) * n_kt + base + __popc(ballot & ((1u << lane) - 1u))] = entry;
         base += __popc(ballot);
     }
-    if (lane == 0 && count) count[qt] = base;
+    if (lane == 0) count[pair] = base;
 }
 
 __global__ void convert_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, int64_t n) {
@@ -595,9 +656,10 @@ cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
 size_t workspace_bytes_for(int64_t seqlen_q, int64_t seqlen_k, bool has_mask) {
     if (!has_mask) return 0;
     const int64_t n_qt = (seqlen_q + kTileQ - 1) / kTileQ;
+    const int64_t n_pairs = (n_qt + 1) / 2;
     const int64_t n_kt = (seqlen_k + kTileK - 1) / kTileK;
-    const size_t list = static_cast<size_t>(n_qt * n_kt) * sizeof(uint32_t);
-    const size_t count = static_cast<size_t>(n_qt) * sizeof(int32_t);
+    const size_t list = static_cast<size_t>(n_pairs * n_kt) * sizeof(uint32_t);
+    const size_t count = static_cast<size_t>(n_pairs) * sizeof(int32_t);
     return ((list + 255) & ~static_cast<size_t>(255)) + ((count + 255) & ~static_cast<size_t>(255));
 }
 
@@ -662,12 +724,13 @@ int* device_status_ptr(int device) {
 }
 
 int launch_tile_map(int32_t m, int32_t n, int32_t causal, const uint8_t* mask, int32_t mqbs, int32_t mkbs,
-                    int32_t mqblocks, int32_t mkblocks, uint32_t* list, int32_t* count, uint8_t* cls_out,
-                    cudaStream_t stream) {
+                    int32_t mqblocks, int32_t mkblocks, uint8_t* cls_out, cudaStream_t stream) {
     const int n_qt = (m + kTileQ - 1) / kTileQ;
     const int n_kt = (n + kTileK - 1) / kTileK;
-    tile_map_kernel<<<n_qt, 32, 0, stream>>>(m, n, n_qt, n_kt, causal, mask, mqbs, mkbs, mqblocks, mkblocks, list,
-                                              count, cls_out);
+    const int64_t total = static_cast<int64_t>(n_qt) * n_kt;
+    const int blocks = static_cast<int>((total + 255) / 256);
+    tile_class_kernel<<<blocks, 256, 0, stream>>>(m, n, n_qt, n_kt, causal, mask, mqbs, mkbs, mqblocks, mkblocks,
+                                                   cls_out);
     return cudaGetLastError() == cudaSuccess ? ODF_OK : ODF_ERR_CUDA;
 }
 
@@ -691,6 +754,7 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
     int rc = ensure_device_ready(device, err);
     if (rc != ODF_OK) return rc;
     a.status = device_status_ptr(device);
+    a.n_pairs = (a.n_qt + 1) / 2;
 
     CUtensorMap tq, tk, tv;
     if (encode_bf16_4d(&tq, L.q, L.head_dim, a.m, a.heads_q, a.batch, L.q_strides) != CUDA_SUCCESS ||
@@ -701,20 +765,20 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
     }
     if (a.mode == kModeList) {
         uint8_t* ws = static_cast<uint8_t*>(L.workspace);
-        const size_t list_bytes = static_cast<size_t>(a.n_qt) * a.n_kt * sizeof(uint32_t);
+        const size_t list_bytes = static_cast<size_t>(a.n_pairs) * a.n_kt * sizeof(uint32_t);
         uint32_t* list = reinterpret_cast<uint32_t*>(ws);
         int32_t* count = reinterpret_cast<int32_t*>(ws + ((list_bytes + 255) & ~static_cast<size_t>(255)));
-        rc = launch_tile_map(a.m, a.n, a.causal, a.mask, a.mask_qbs, a.mask_kbs, a.mask_qblocks, a.mask_kblocks,
-                             list, count, nullptr, stream);
-        if (rc != ODF_OK) {
+        pair_list_kernel<<<a.n_pairs, 32, 0, stream>>>(a.m, a.n, a.n_pairs, a.n_kt, a.causal, a.mask, a.mask_qbs,
+                                                        a.mask_kbs, a.mask_qblocks, a.mask_kblocks, list, count);
+        if (cudaGetLastError() != cudaSuccess) {
             *err = "tile-list kernel launch failed";
-            return rc;
+            return ODF_ERR_CUDA;
         }
         a.tile_list = list;
         a.tile_count = count;
     }
     const int mod = (L.has_alibi ? kModAlibi : 0) | (L.has_softcap ? kModSoftcap : 0);
-    const dim3 grid(static_cast<unsigned>(a.batch * a.heads_q), static_cast<unsigned>(a.n_qt), 1);
+    const dim3 grid(static_cast<unsigned>(a.batch * a.heads_q), static_cast<unsigned>(a.n_pairs), 1);
     cudaError_t e = (L.head_dim == 64) ? launch_d<64>(tq, tk, tv, a, mod, grid, stream)
                                        : launch_d<128>(tq, tk, tv, a, mod, grid, stream);
     if (e != cudaSuccess) {

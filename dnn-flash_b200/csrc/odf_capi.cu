@@ -374,8 +374,8 @@ int odf_tile_map_sm100(int64_t seqlen_q, int64_t seqlen_k, int32_t causal, const
                                         block_mask, static_cast<int32_t>(std::min<int64_t>(mask_qbs, 0x7fffffff)),
                                         static_cast<int32_t>(std::min<int64_t>(mask_kbs, 0x7fffffff)),
                                         static_cast<int32_t>(std::min<int64_t>(mask_qblocks, 0x7fffffff)),
-                                        static_cast<int32_t>(std::min<int64_t>(mask_kblocks, 0x7fffffff)), nullptr,
-                                        nullptr, out, static_cast<cudaStream_t>(stream));
+                                        static_cast<int32_t>(std::min<int64_t>(mask_kblocks, 0x7fffffff)), out,
+                                        static_cast<cudaStream_t>(stream));
     if (rc != ODF_OK) return fail(rc, "tile map kernel launch failed");
     return ODF_OK;
 }

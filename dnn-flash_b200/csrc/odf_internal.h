@@ -19,8 +19,13 @@ enum TileMode : int32_t {
     kModeList = 2,    // compacted per-query-tile list built from the block mask
 };
 
-// Flags carried in the upper half of a tile-list entry (low 16 bits = kv tile index).
-constexpr uint32_t kListBitmapPartial = 1u << 16;  // some covered mask block is disallowed
+// A KV-list entry of a query-tile pair: kv tile index in the low 16 bits, then
+// which of the pair's two query tiles need the KV tile and which of them must test
+// the BlockMask bitmap per element (a covered mask block is disallowed).
+constexpr uint32_t kNeed0 = 1u << 16;
+constexpr uint32_t kNeed1 = 1u << 17;
+constexpr uint32_t kBitmap0 = 1u << 18;
+constexpr uint32_t kBitmap1 = 1u << 19;
 
 // Everything the forward kernel needs besides the three tensor maps.
 struct FwdArgs {
@@ -29,7 +34,7 @@ struct FwdArgs {
     int64_t o_stride_b, o_stride_h, o_stride_t;  // elements
     int32_t o_bf16;
     int32_t batch, heads_q, heads_kv, m, n;
-    int32_t n_qt, n_kt;
+    int32_t n_qt, n_kt, n_pairs;
     int32_t mode;
     int32_t causal;
     float scale;        // natural-units softmax scale
@@ -38,8 +43,8 @@ struct FwdArgs {
     float inv_softcap;
     const uint8_t* mask;
     int32_t mask_qbs, mask_kbs, mask_qblocks, mask_kblocks;
-    const uint32_t* tile_list;  // [n_qt, n_kt]
-    const int32_t* tile_count;  // [n_qt]
+    const uint32_t* tile_list;  // [n_pairs, n_kt]
+    const int32_t* tile_count;  // [n_pairs]
     uint8_t* visits;
     int* status;
     int32_t alibi_generated;    // slopes = 2^(-8 (h+1) / heads_q)
@@ -64,10 +69,9 @@ struct FwdLaunch {
 // Returns ODF_OK or an ODF_ERR_* code; `err` receives a message on failure.
 int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err);
 
-// Tile classification kernel for odf_tile_map_sm100 / the workspace lists.
+// Per-query-tile classification kernel for odf_tile_map_sm100.
 int launch_tile_map(int32_t m, int32_t n, int32_t causal, const uint8_t* mask, int32_t mqbs, int32_t mkbs,
-                    int32_t mqblocks, int32_t mkblocks, uint32_t* list, int32_t* count, uint8_t* cls_out,
-                    cudaStream_t stream);
+                    int32_t mqblocks, int32_t mkblocks, uint8_t* cls_out, cudaStream_t stream);
 
 // fp32 -> bf16 conversion kernel.
 int launch_convert_f32_bf16(const float* in, uint16_t* out, int64_t count, cudaStream_t stream);
