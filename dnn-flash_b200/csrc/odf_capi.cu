@@ -410,3 +410,63 @@ const char* odf_last_error(void) { return t_last_error.c_str(); }
 const char* odf_version(void) { return "dnn-flash-b200 0.1.0 (sm_100a tcgen05/TMA forward)"; }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ no-allocation entry
+// Scratch for odf_flash_fwd_sm100_noalloc: a fixed-size array in the module's device
+// memory, present on every GPU that loads this library until the process exits.
+// Host code must not use the symbol itself as a pointer (on the host it only names a
+// stand-in); its device address is looked up once per device below.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[ODF_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+struct NoAllocDevice {
+    bool ready = false;
+    void* scratch = nullptr;
+};
+NoAllocDevice g_noalloc[64];
+std::mutex g_noalloc_mutex;
+
+// Resolves the device address of g_noalloc_scratch for the current device (first call only).
+int noalloc_scratch_for_current_device(void** out) {
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail(ODF_ERR_NO_DEVICE, "no CUDA device");
+    if (device < 0 || device >= 64) return fail(ODF_ERR_NO_DEVICE, "device index out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    NoAllocDevice& d = g_noalloc[device];
+    if (!d.ready) {
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || ptr == nullptr)
+            return fail(ODF_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch) failed: ") + cudaGetErrorString(e));
+        d.scratch = ptr;
+        d.ready = true;
+    }
+    *out = d.scratch;
+    return ODF_OK;
+}
+
+}  // namespace
+
+extern "C" int odf_flash_fwd_sm100_noalloc(const odf_fwd_params* p, void* stream) {
+    Resolved r;
+    int rc = validate(p, false, &r);
+    if (rc != ODF_OK) return rc;
+    const size_t need = odf::workspace_bytes_for(p->seqlen_q, p->seqlen_k, p->block_mask != nullptr);
+    if (need > ODF_NOALLOC_SCRATCH_BYTES)
+        return fail(ODF_ERR_UNSUPPORTED, "block-mask tile lists need " + std::to_string(need) +
+                                             " bytes of scratch; odf_flash_fwd_sm100_noalloc has " +
+                                             std::to_string(ODF_NOALLOC_SCRATCH_BYTES) +
+                                             " (use odf_flash_fwd_sm100 with a workspace)");
+    odf_fwd_params q = *p;
+    q.workspace = nullptr;
+    q.workspace_bytes = 0;
+    if (need > 0) {
+        void* scratch = nullptr;
+        rc = noalloc_scratch_for_current_device(&scratch);
+        if (rc != ODF_OK) return rc;
+        q.workspace = scratch;
+        q.workspace_bytes = ODF_NOALLOC_SCRATCH_BYTES;
+    }
+    return run_device(&q, r, static_cast<cudaStream_t>(stream));
+}

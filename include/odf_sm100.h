@@ -94,6 +94,31 @@ int odf_flash_fwd_sm100(const odf_fwd_params* p, void* stream);
    (src/onednn_flash/attention_workspace.cpp:5-20). */
 size_t odf_fwd_workspace_size(const odf_fwd_params* p);
 
+/* Capacity of the library-owned scratch used by odf_flash_fwd_sm100_noalloc. */
+#define ODF_NOALLOC_SCRATCH_BYTES (1u << 20)
+
+/*
+ * Same forward pass as odf_flash_fwd_sm100, for callers that cannot allocate
+ * device memory: code that runs where cudaMalloc is not allowed or not wanted
+ * (a serving loop with a fixed memory budget where an allocation would
+ * synchronise the device or fail, a plugin whose host framework owns the
+ * allocator, a foreign-language binding with no allocator of its own).  The
+ * caller still passes Q/K/V, O and LSE; p->workspace is ignored.
+ *
+ * Instead of a caller workspace, the block-mask tile lists go to a fixed array
+ * of ODF_NOALLOC_SCRATCH_BYTES in this library's device memory (held by every
+ * GPU that loads the library until the process exits).  Limit: the lists take
+ * about ceil(seqlen_q/256) * ceil(seqlen_k/128) * 4 bytes; larger problems are
+ * rejected with ODF_ERR_UNSUPPORTED.  Without a block mask no scratch is used.
+ * The first call on a device looks up the array's device address (a one-time,
+ * non-allocating runtime call); make that first call before any stream capture.
+ * All calls share the one array and nothing in it needs to start at zero (each
+ * launch rewrites the lists it reads), but calls that overlap on the GPU, on
+ * different streams, race on it: serialise them.
+ * No counterpart in the reference (its workspace is always caller-owned).
+ */
+int odf_flash_fwd_sm100_noalloc(const odf_fwd_params* p, void* stream);
+
 /*
  * Forward pass on HOST buffers (pageable or pinned) through the current
  * device; blocks until the result is in `p->o` / `p->lse`.  Q/K/V may be

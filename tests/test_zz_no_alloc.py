@@ -1,0 +1,111 @@
+"""odf_flash_fwd_sm100_noalloc: the entry point for callers that cannot allocate
+device memory (fixed-budget serving loops, plugins whose host owns the allocator,
+foreign-language bindings without an allocator).  It keeps its block-mask tile lists
+in a library-owned static device array instead of a caller workspace.
+
+Checked through the C ABI against odf_flash_fwd_sm100 (which uses a caller
+workspace) on the same inputs, on two calls in a row so that a second call over
+the scratch left by the first is covered too.  This file is collected last so a
+failure here never hides the rest of the suite.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import make_qkv
+
+pytestmark = pytest.mark.gpu
+
+O_REL_L2 = 1e-2
+O_MAX_ABS = 2e-2
+LSE_MAX_ABS = 1e-3
+
+
+def _lib():
+    import odf_b200
+
+    lib = odf_b200.load_library()
+    lib.odf_flash_fwd_sm100_noalloc.argtypes = [C.POINTER(odf_b200.FwdParams), C.c_void_p]
+    lib.odf_flash_fwd_sm100_noalloc.restype = C.c_int
+    return lib
+
+
+def _run(entry, q, k, v, mask, mask_block, causal, use_workspace):
+    import odf_b200
+    import torch
+
+    B, Hq, M, D = q.shape
+    o = torch.full((B, Hq, M, v.shape[3]), float("nan"), dtype=torch.float32, device="cuda")
+    lse = torch.full((B, Hq, M), float("nan"), dtype=torch.float32, device="cuda")
+    mask_t = torch.as_tensor(mask, dtype=torch.uint8).cuda().contiguous() if mask is not None else None
+    p, keep = odf_b200.fill_params(q, k, v, o, lse, causal=causal, scale=1.0 / np.sqrt(D), block_mask=mask_t,
+                                   mask_block=mask_block, alibi=False, alibi_slopes_host=None, softcap=0.0,
+                                   workspace=None, visits=None)
+    ws = None
+    if use_workspace:
+        nbytes = _lib().odf_fwd_workspace_size(C.byref(p))
+        if nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+            p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
+    rc = entry(C.byref(p), C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, odf_b200.last_error()
+    torch.cuda.synchronize()
+    del keep, ws
+    return o.cpu().numpy(), lse.cpu().numpy()
+
+
+def _compare(o, lse, o_ref, lse_ref):
+    diff = o.astype(np.float64) - o_ref.astype(np.float64)
+    assert np.linalg.norm(diff) / max(np.linalg.norm(o_ref), 1e-30) <= O_REL_L2
+    assert np.abs(diff).max() <= O_MAX_ABS
+    fin = np.isfinite(lse_ref)
+    assert np.array_equal(np.isfinite(lse), fin)
+    assert np.abs(lse[fin] - lse_ref[fin]).max() <= LSE_MAX_ABS
+
+
+@pytest.mark.parametrize("case", ["block_mask_causal", "block_mask_small_blocks", "causal_no_mask"])
+def test_noalloc_matches_workspace_entry_two_calls(case):
+    import torch
+
+    import oracle
+
+    lib = _lib()
+    if case == "block_mask_causal":
+        mask, mb, causal, n = oracle.sliding_window_prefix_mask(10, 3, 2), (128, 128), True, 1280
+    elif case == "block_mask_small_blocks":
+        rng = np.random.default_rng(3)
+        mask, mb, causal, n = (rng.random((20, 15)) > 0.4).astype(np.uint8), (48, 64), False, 900
+    else:
+        mask, mb, causal, n = None, (128, 128), True, 700
+    results = []
+    for call in range(2):
+        qn, kn, vn = make_qkv(40 + call, 2, 4, 2, n, n, 128)
+        q, k, v = (torch.from_numpy(x).cuda().to(torch.bfloat16) for x in (qn, kn, vn))
+        o_ref, lse_ref = _run(lib.odf_flash_fwd_sm100, q, k, v, mask, mb, causal, use_workspace=True)
+        o, lse = _run(lib.odf_flash_fwd_sm100_noalloc, q, k, v, mask, mb, causal, use_workspace=False)
+        _compare(o, lse, o_ref, lse_ref)
+        results.append(o)
+    assert not np.array_equal(results[0], results[1])  # the two calls really ran on different inputs
+
+
+def test_noalloc_rejects_lists_beyond_scratch():
+    import odf_b200
+    import torch
+
+    lib = _lib()
+    # 131072 x 131072 with a block mask needs 512 * 1024 * 4 bytes of lists > 1 MiB
+    p = odf_b200.FwdParams()
+    t = torch.zeros(16, dtype=torch.bfloat16, device="cuda")
+    p.q = p.k = p.v = p.o = t.data_ptr()
+    p.qkv_dtype, p.o_dtype = odf_b200.ODF_DTYPE_BF16, odf_b200.ODF_DTYPE_F32
+    p.batch, p.heads_q, p.heads_kv, p.seqlen_q, p.seqlen_k, p.head_dim, p.value_dim = 1, 1, 1, 131072, 131072, 64, 64
+    p.scale = 0.125
+    p.block_mask = t.data_ptr()
+    p.mask_qbs = p.mask_kbs = 128
+    p.mask_qblocks = p.mask_kblocks = 1
+    rc = lib.odf_flash_fwd_sm100_noalloc(C.byref(p), None)
+    assert rc == odf_b200.ODF_ERR_UNSUPPORTED
+    assert "scratch" in odf_b200.last_error()
