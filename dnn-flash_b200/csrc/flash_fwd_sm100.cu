@@ -394,9 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int t = 0; t < 8; ++t) mx8[t] = s[t];
 #pragma unroll
-            for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-            float tile_max = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            for (int c = 8; c < 128; c += 2) mx8[(c >> 1) & 7] = ptx::fmax3(mx8[(c >> 1) & 7], s[c], s[c + 1]);
+            float tile_max = ptx::fmax3(ptx::fmax3(mx8[0], mx8[1], mx8[2]), ptx::fmax3(mx8[3], mx8[4], mx8[5]),
+                                        fmaxf(mx8[6], mx8[7]));
             if (raw) tile_max *= args.scale_log2;
             float alpha = 1.0f;
             if (m_run == -INFINITY) {
@@ -406,33 +406,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m_run = tile_max;
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            float sum8[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) sum8[t] = 0.0f;
-            // P (bf16 pairs) is packed in place into s[0..63]: element c/2 is written only
-            // after s[c] and s[c+1] were consumed, so no second register array is needed.
-            if (raw) {
-                const float neg = -m_use;
-#pragma unroll
-                for (int c = 0; c < 128; c += 2) {
-                    const float p0 = ptx::ex2(fmaf(s[c], args.scale_log2, neg));
-                    const float p1 = ptx::ex2(fmaf(s[c + 1], args.scale_log2, neg));
-                    sum8[c & 7] += p0;
-                    sum8[(c + 1) & 7] += p1;
-                    s[c >> 1] = __uint_as_float(ptx::pack_bf16x2(p0, p1));
-                }
-            } else {
+            // P = 2^(x - m) on fp32 pairs; the bf16 pairs are packed in place into s[0..63]
+            // (element c/2 is written only after s[c] and s[c+1] were consumed).
+            uint64_t sum2[4] = {0, 0, 0, 0};
+            {
+                const uint64_t mul2 = ptx::f32x2(raw ? args.scale_log2 : 1.0f);
+                const uint64_t neg2 = ptx::f32x2(-m_use);
 #pragma unroll
                 for (int c = 0; c < 128; c += 2) {
-                    const float p0 = ptx::ex2(s[c] - m_use);
-                    const float p1 = ptx::ex2(s[c + 1] - m_use);
-                    sum8[c & 7] += p0;
-                    sum8[(c + 1) & 7] += p1;
+                    const uint64_t x = ptx::ffma2(ptx::f32x2(s[c], s[c + 1]), mul2, neg2);
+                    const float p0 = ptx::ex2(ptx::lo_f32(x));
+                    const float p1 = ptx::ex2(ptx::hi_f32(x));
+                    sum2[(c >> 1) & 3] = ptx::fadd2(sum2[(c >> 1) & 3], ptx::f32x2(p0, p1));
                     s[c >> 1] = __uint_as_float(ptx::pack_bf16x2(p0, p1));
                 }
             }
-            l_run = l_run * alpha +
-                    (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
+            const uint64_t sum_all = ptx::fadd2(ptx::fadd2(sum2[0], sum2[1]), ptx::fadd2(sum2[2], sum2[3]));
+            l_run = l_run * alpha + (ptx::lo_f32(sum_all) + ptx::hi_f32(sum_all));
 
             // correction: O_i *= alpha when the reference max moved (PV_i of the previous
             // tile is complete: the commit that released S_i(j) covers every earlier MMA)

@@ -57,16 +57,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the warp for up to `hint_ns` while the
+// phase is incomplete, so waiting warps do not take issue slots from the warps
+// computing on the same SM sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity.  Gives up after `limit_ns`
 // or as soon as another role of the CTA has raised `abort_flag`; on its own
 // timeout it raises the flag and records `code` in the device status word.
+// Between checks the warp sleeps in try_wait (suspend hint of 0.5 ms).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, int code, uint64_t limit_ns) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (mbar_try_wait(a, parity)) return true;
+        if (mbar_try_wait_sleep(a, parity, 500000u)) return true;
         if (*abort_flag) return false;
         if (global_timer_ns() - t0 > limit_ns) {
             *abort_flag = 1;
@@ -245,6 +261,33 @@ __device__ __forceinline__ float rcp(float x) {
     float y;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): lo in bits [0,32), hi in [32,64).
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+    return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t f32x2(float v) { return f32x2(v, v); }
+__device__ __forceinline__ float lo_f32(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi_f32(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// Three-input max (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
