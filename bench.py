@@ -161,6 +161,46 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def shard_config(cfg, rank, world, scaling):
+    """The rank's share of the workload and its input seed.
+
+    weak:   every rank runs the whole configuration on its own inputs (batch element
+            `rank` of a global batch of `world`), so per-GPU work is fixed.
+    strong: the configuration's (batch, kv-head group) units are split contiguously
+            across ranks; a rank keeps whole GQA groups, so no K/V crosses ranks.
+    """
+    if scaling == "weak":
+        return dict(cfg), 1234 + rank
+    units = cfg["B"] * cfg["Hkv"]
+    if units % world != 0:
+        raise ValueError(f"{units} (batch x kv-head) units do not split over {world} ranks")
+    per = units // world
+    group = cfg["Hq"] // cfg["Hkv"]
+    out = dict(cfg)
+    if per % cfg["Hkv"] == 0:          # whole batch elements per rank
+        out["B"] = per // cfg["Hkv"]
+    elif cfg["Hkv"] % per == 0:        # a slice of one batch element's kv heads
+        out["B"] = 1
+        out["Hkv"] = per
+        out["Hq"] = per * group
+    else:
+        raise ValueError(f"{per} units per rank do not form a [B, H] block")
+    return out, 1234 + rank
+
+
+def reduce_max(values, dist):
+    """Element-wise max over ranks of a list of floats (device timing is max over GPUs)."""
+    import torch
+
+    if dist is None:
+        return [float(v) for v in values]
+    backend = dist.get_backend()
+    dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.cpu()]
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -268,9 +308,10 @@ def run_ours(args, cfg, workload):
         torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
 
+    cfg, seed = shard_config(cfg, rank, world, args.scaling)
     B, Hq, Hkv, N, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["N"], cfg["D"]
     out_dtype = torch.bfloat16 if cfg["out"] == "bf16" else torch.float32
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    g = torch.Generator(device=dev).manual_seed(seed)
     s = cfg["in_scale"]
     q = (torch.randn((B, Hq, N, D), generator=g, device=dev) * s).to(torch.bfloat16)
     k = (torch.randn((B, Hkv, N, D), generator=g, device=dev) * s).to(torch.bfloat16)
@@ -340,13 +381,10 @@ def run_ours(args, cfg, workload):
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
     d2h = ho.numel() * ho.element_size() + hl.numel() * 4
 
-    vals = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, e2e_s = float(vals[0]), float(vals[1])
+    total_ms, e2e_s = reduce_max([total_ms, e2e_s], dist)
 
     peak, peak_sus, hbm, peak_kind = measured_peaks()
-    value = world * flop_rank * args.steps / (total_ms * 1e-3) / 1e12
+    value = world * flop_rank * args.steps / (total_ms * 1e-3) / 1e12  # every rank runs the same FLOP
     avg_launch_ms = statistics.mean(per_launch_ms)
     achieved = flop_rank / (avg_launch_ms * 1e-3) / 1e12
     result = None
@@ -360,13 +398,14 @@ def run_ours(args, cfg, workload):
             "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": args.scaling,
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
             "config": {
                 "workload": workload,
-                "batch_per_gpu": B, "global_batch": B * world, "heads_q": Hq, "heads_kv": Hkv, "seq_len": N,
+                "batch_per_gpu": B, "global_batch": B * world if args.scaling == "weak" else CONFIGS[args.config]["B"],
+                "heads_q_per_gpu": Hq, "heads_kv_per_gpu": Hkv, "seq_len": N,
                 "head_dim": D, "causal": cfg["causal"], "alibi": cfg["alibi"], "softcap": cfg["softcap"],
                 "block_mask": cfg["mask"], "out_dtype": cfg["out"], "lse": True,
                 "parallelism": f"(batch x head) shards, {world} GPU(s), no collective on the data path",
@@ -385,8 +424,8 @@ def run_ours(args, cfg, workload):
                 "kernel": "flash_fwd_kernel<128,0>",
                 "avg_launch_ms": avg_launch_ms,
             },
-            "e2e": {"value": world * flop_rank / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "path": "odf_flash_fwd_host (pinned host buffers)"},
+            "e2e": {"value": world * flop_rank / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world, "path": "odf_flash_fwd_host (pinned host buffers)"},
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(),
         }
@@ -415,6 +454,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=3072, help="prefix rows of the CPU baseline sample")
     ap.add_argument("--ref-rows", type=int, default=1536, help="prefix rows per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="weak: the config per GPU (default); strong: the config split over the GPUs")
     ap.add_argument("--seq-len", type=int, default=None,
                     help="override N (profiling of a smaller case only; the BASELINE config is the default)")
     args = ap.parse_args()

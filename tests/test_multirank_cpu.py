@@ -1,0 +1,77 @@
+"""Host-side multi-GPU logic of bench.py with world_size-2 gloo ranks on CPU.
+
+Heads are independent, so the data path has no collective: each rank gets a shard
+(weak: the whole config on its own inputs; strong: contiguous (batch, kv-head) groups)
+and the only collective is the max-over-ranks of the timed region.
+"""
+from __future__ import annotations
+
+import json
+import os
+import socket
+import sys
+
+import pytest
+import torch.multiprocessing as mp
+
+from conftest import ROOT
+
+sys.path.insert(0, str(ROOT))
+import bench  # noqa: E402
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        shards = {name: bench.shard_config(cfg, rank, world, "strong")[0] for name, cfg in bench.CONFIGS.items()
+                  if (cfg["B"] * cfg["Hkv"]) % world == 0}
+        weak_cfg, weak_seed = bench.shard_config(bench.CONFIGS["c5"], rank, world, "weak")
+        timing = bench.reduce_max([10.0 + rank, 5.0 - rank], dist)
+        dist.barrier()
+        with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
+            json.dump({"shards": shards, "weak": weak_cfg, "seed": weak_seed, "timing": timing}, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_shard_and_reduce(tmp_path):
+    world = 2
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    res = [json.loads((tmp_path / f"rank{r}.json").read_text()) for r in range(world)]
+    # max over ranks, identical on every rank
+    assert res[0]["timing"] == res[1]["timing"] == [11.0, 5.0]
+    # weak scaling: whole config per rank, distinct input seeds
+    assert res[0]["weak"] == res[1]["weak"] == bench.CONFIGS["c5"]
+    assert res[0]["seed"] != res[1]["seed"]
+    # strong scaling: the ranks' FLOP add up to the whole config's
+    for name, cfg in bench.CONFIGS.items():
+        if name not in res[0]["shards"]:
+            continue
+        total = bench.flop_per_unit_pairs(cfg) * cfg["B"] * cfg["Hq"]
+        parts = sum(bench.flop_per_unit_pairs(r["shards"][name]) * r["shards"][name]["B"] * r["shards"][name]["Hq"]
+                    for r in res)
+        assert parts == total, name
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_strong_shards_keep_whole_gqa_groups(world):
+    cfg = bench.CONFIGS["c5"]
+    shard, _ = bench.shard_config(cfg, 0, world, "strong")
+    assert shard["Hq"] // shard["Hkv"] == cfg["Hq"] // cfg["Hkv"]
+    assert shard["Hkv"] * world == cfg["Hkv"]
+
+
+def test_strong_sharding_rejects_uneven_split():
+    with pytest.raises(ValueError):
+        bench.shard_config(bench.CONFIGS["c1"], 0, 3, "strong")
