@@ -93,11 +93,34 @@ __device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, int pair, int j, 
     return e;
 }
 
-__device__ __forceinline__ bool mask_allows(const FwdArgs& a, int qi, int kj) {
+// Bits of the 128 columns [k0, k0+128) that the BlockMask allows for query row qi
+// (attention.cpp:70-86; blocks outside the bitmap are disallowed).  Walks the few mask
+// blocks the tile spans instead of testing every column.
+__device__ __forceinline__ uint4 row_allow_bits(const FwdArgs& a, int qi, int k0) {
+    uint4 allow = make_uint4(0u, 0u, 0u, 0u);
     const int qb = qi / a.mask_qbs;
-    const int kb = kj / a.mask_kbs;
-    if (qb >= a.mask_qblocks || kb >= a.mask_kblocks) return false;
-    return __ldg(a.mask + static_cast<int64_t>(qb) * a.mask_kblocks + kb) != 0;
+    if (qb >= a.mask_qblocks) return allow;
+    const uint8_t* mrow = a.mask + static_cast<int64_t>(qb) * a.mask_kblocks;
+#pragma unroll 1
+    for (int kb = k0 / a.mask_kbs; kb < a.mask_kblocks; ++kb) {
+        const int c0 = max(kb * a.mask_kbs - k0, 0);
+        if (c0 >= kTileK) break;
+        const int c1 = min((kb + 1) * a.mask_kbs - k0, kTileK);  // exclusive
+        if (__ldg(mrow + kb) == 0) continue;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {  // the block's columns [c0, c1) within word w
+            const int lo = min(max(c0 - 32 * w, 0), 32);
+            const int hi = min(max(c1 - 32 * w, 0), 32);
+            const uint32_t upto = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
+            const uint32_t from = lo >= 32 ? 0u : ~((1u << lo) - 1u);
+            const uint32_t bits = upto & from;
+            if (w == 0) allow.x |= bits;
+            if (w == 1) allow.y |= bits;
+            if (w == 2) allow.z |= bits;
+            if (w == 3) allow.w |= bits;
+        }
+    }
+    return allow;
 }
 
 // Accurate tanh from the identity tanh(t) = 1 - 2 / (1 + e^(2t)); absolute error
@@ -374,18 +397,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 0; c < 128; ++c) s[c] *= args.scale_log2;
             }
 
-            // element mask on boundary tiles (attention.cpp:54-62, 608-617)
+            // element mask on boundary tiles (attention.cpp:54-62, 608-617): column c of the
+            // tile survives iff c <= limit (causal kj <= qi, ragged kj < N) and, on tiles that
+            // cover a disallowed BlockMask block, its bit in the row's 128-bit allow mask.
             const bool ragged = (k0 + kTileK > args.n);
             const bool diag = args.causal && (min(args.n, k0 + kTileK) - 1 > q0);
             const bool bitmap = (e & bitmap_bit) != 0;
             if (ragged || diag || bitmap) {
+                int limit = args.n - 1 - k0;
+                if (args.causal) limit = min(limit, qi - k0);
+                const uint4 allow = bitmap ? row_allow_bits(args, qi, k0)
+                                           : make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
 #pragma unroll
                 for (int c = 0; c < 128; ++c) {
-                    const int kj = k0 + c;
-                    bool masked = kj >= args.n;
-                    if (args.causal) masked = masked || (kj > qi);
-                    if (bitmap) masked = masked || !mask_allows(args, qi, kj);
-                    if (masked) s[c] = -INFINITY;
+                    const uint32_t word = (c < 32) ? allow.x : (c < 64) ? allow.y : (c < 96) ? allow.z : allow.w;
+                    const bool keep = (c <= limit) && ((word >> (c & 31)) & 1u);
+                    s[c] = keep ? s[c] : -INFINITY;
                 }
             }
 
