@@ -1,25 +1,34 @@
 // flash_fwd_sm100.cu -- tiled attention forward for B200 (sm_100a).
 //
-// One CTA computes a PAIR of 128-row query tiles (Q0, Q1) of one (batch, q-head)
-// and walks the KV tiles the tiling does not skip, loading each K/V tile once for
-// both query tiles.  It replaces the query-block and key-block loops of the
+// Persistent kernel: one CTA per SM walks a fixed sequence of work items (ItemSchedule).
+// An item is a PAIR of 128-row query tiles (Q0, Q1) of one (batch, q-head); the CTA
+// walks the KV tiles the tiling does not skip, loading each K/V tile once for both
+// query tiles.  The K/V ring, the barriers' phases and the TMEM allocation carry over
+// from item to item, so the next item's Q load and first S MMAs overlap the current
+// item's last P.V and its epilogue.  It replaces the query-block and key-block loops of the
 // reference's flash_attention_qk_pv_tile_ws (src/onednn_flash/attention.cpp:513-688):
 // the scalar tile GEMMs (tile_kernel.cpp:57-85) become tcgen05 MMAs fed by TMA and
 // accumulating in tensor memory, and the per-row online softmax
 // (attention.cpp:602-674) runs in registers, one thread per query row.
 //
-// Warp roles (320 threads):
+// Warp roles (384 threads, three warpgroups):
 //   warps 0-3  softmax of Q0 (+ its epilogue); thread t owns row t = TMEM lane t
 //   warps 4-7  softmax of Q1 (+ its epilogue)
-//   warp  8    TMA producer (Q0/Q1 once, then K_j, V_j through a ring of slots);
+//   warp  8    TMA producer (Q0/Q1 per item, K_j, V_j through a ring of slots);
 //              it also owns the TMEM allocation
 //   warp  9    MMA issuer (one thread)
+//   warps 10-11 idle
+// setmaxnreg moves registers from warpgroup 2 (168 -> 88) to the softmax warpgroups
+// (168 -> 208), which hold a whole 128-column S row per thread.  The roles never meet in
+// common code after the split (each ends with its own CTA barrier), so ptxas allocates
+// each under its own budget.
 // Tensor memory (512 columns):
 //   S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D,256+2D)
 //   P_i (bf16, two per column) is written over the first 64 columns of S_i and is
 //   the A operand of the P.V MMA read straight from tensor memory.
 // MMA issue order per KV tile j (in-order execution on the tensor core):
 //   PV0(j), S0(j+1), PV1(j), S1(j+1)
+// and at an item's last tile PV0, PV1 (committed to o_done[0/1]) then S0, S1 of the next item
 // so while the softmax of one query tile runs, the tensor core works on the other
 // tile's P.V and S MMAs.  S_i(j+1) overwrites S_i/P_i only after PV_i(j) was issued.
 // The softmax raises its running max only when a tile's max exceeds it by more than
@@ -43,9 +52,18 @@ namespace odf {
 
 namespace {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;  // three warpgroups
 constexpr int kWarpProducer = 8;
-constexpr int kWarpMma = 9;
+constexpr int kWarpMma = 9;    // warps 10 and 11 only give their registers away
+// Register split: the kernel is compiled for kLaunchRegs per thread (three warps share an
+// SMSP); warpgroup 2 drops to kRegsCtrl and the two softmax warpgroups rise to
+// kRegsSoftmax, which must not exceed what the block was launched with.  The host checks
+// the compiled register count before the first launch.
+constexpr int kLaunchRegs = 168;
+constexpr int kRegsCtrl = 88;
+constexpr int kRegsSoftmax = 208;
+static_assert(128 * kRegsCtrl + 256 * kRegsSoftmax <= kThreads * kLaunchRegs, "register split exceeds the launch");
+static_assert(kRegsCtrl % 8 == 0 && kRegsSoftmax % 8 == 0 && kRegsSoftmax <= 256, "setmaxnreg operands");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kChunkBytes = 128 * 128;  // 128 rows x 128 bytes (64 bf16)
@@ -64,20 +82,35 @@ struct Config {
     static constexpr uint32_t kTileBytes = 128 * D * 2;
     static constexpr uint32_t kOffSlots = 2 * kTileBytes;
     static constexpr uint32_t kOffBar = kOffSlots + kSlots * kTileBytes;
-    static constexpr int kNumBars = 1 + 2 * kSlots + 2 + 2 + 1 + 1;
-    static constexpr uint32_t kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
+    static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 1;
+    static constexpr uint32_t kOffRows = kOffBar + kNumBars * 8 + 16;  // after the barriers, TMEM slot, abort flag
+    static constexpr uint32_t kSmemBytes = kOffRows + 8 * 32 + 1024;     // + alignment slack
     static constexpr uint32_t kTmemO = 256;
 };
 
 struct Bars {
     uint64_t* q_full;
+    uint64_t* q_empty;
     uint64_t* slot_full;
     uint64_t* slot_empty;
     uint64_t* s_full;   // [2]
     uint64_t* p_full;   // [2]
-    uint64_t* mma_done;
+    uint64_t* o_done;   // [2]
     uint64_t* drain;
 };
+
+// The current item as one softmax warp sees it, kept in shared memory (one record per
+// warp, written by lane 0) and read where needed, so that no registers stay tied up
+// across the softmax loop.
+struct RowItem {
+    int n_entries;  // KV tiles of the pair
+    int pair;
+    int q0;         // first row of this warp's query tile
+    int n_iter;     // list mode: n_entries; dense/causal: the KV tiles this query tile needs (0..n_iter-1)
+    int bh, b, h;
+    float slope;    // ALiBi slope of head h
+};
+static_assert(sizeof(RowItem) == 32, "RowItem layout");
 
 // KV tile j of this query-tile pair: kv index in the low 16 bits, kNeed*/kBitmap* flags above.
 __device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, int pair, int j, bool valid1, int qend0, int qend1) {
@@ -92,6 +125,72 @@ __device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, int pair, int j, 
     }
     return e;
 }
+
+// One work item: a pair of 128-row query tiles (Q0, Q1) of one (batch, q-head).
+struct Item {
+    int bh, b, h, hk, pair;
+    int q00, q01;      // first rows of Q0 and Q1
+    int qend0, qend1;  // their row ends (clipped to M)
+    int n_entries;     // KV tiles visited by the pair
+    bool valid1;       // Q1 has rows
+};
+
+// Item k covers query-tile pair n_pairs-1-k/(B Hq) of head k mod (B Hq): all heads of the
+// pair with the longest causal rows first.
+__device__ __forceinline__ Item decode_item(const FwdArgs& a, int64_t k) {
+    const int64_t n_bh = static_cast<int64_t>(a.batch) * a.heads_q;
+    const int64_t round = k / n_bh;
+    Item I;
+    I.bh = static_cast<int>(k - round * n_bh);
+    I.pair = a.n_pairs - 1 - static_cast<int>(round);
+    I.b = I.bh / a.heads_q;
+    I.h = I.bh - I.b * a.heads_q;
+    I.hk = I.h / (a.heads_q / a.heads_kv);
+    I.q00 = I.pair * 2 * kTileQ;
+    I.q01 = I.q00 + kTileQ;
+    I.valid1 = I.q01 < a.m;
+    I.qend0 = min(a.m, I.q00 + kTileQ);
+    I.qend1 = I.valid1 ? min(a.m, I.q01 + kTileQ) : I.qend0;
+    if (a.mode == kModeList) {
+        I.n_entries = a.tile_count[I.pair];
+    } else if (a.mode == kModeCausal) {
+        I.n_entries = min(a.n_kt, (I.qend1 + kTileK - 1) / kTileK);
+    } else {
+        I.n_entries = a.n_kt;
+    }
+    return I;
+}
+
+__device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, const Item& I, int j) {
+    return kv_entry(a, I.pair, j, I.valid1, I.qend0, I.qend1);
+}
+
+// Persistent schedule: the grid has G <= #SM CTAs and CTA c takes one item per round,
+// the c-th of round r when r is even and the (G-1-c)-th when r is odd.  Items are sorted by
+// decreasing causal work, so this snake order evens out long and short items the way the
+// hardware's greedy block scheduler would, and every role of the CTA derives the same
+// sequence without communicating.
+struct ItemSchedule {
+    int64_t n_items;
+    __device__ explicit ItemSchedule(const FwdArgs& a)
+        : n_items(static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs) {}
+    // Item index of this CTA's round `it`, or -1 once the CTA has no items left.
+    __device__ __forceinline__ int64_t item(int it) const {
+        const int64_t g = gridDim.x;
+        const int64_t c = (it & 1) ? (g - 1 - blockIdx.x) : blockIdx.x;
+        const int64_t k = static_cast<int64_t>(it) * g + c;
+        return k < n_items ? k : -1;
+    }
+    // Advances `it` to this CTA's next item that visits at least one KV tile.
+    __device__ __forceinline__ bool next_nonempty(const FwdArgs& a, int& it, Item& I) const {
+        for (;;) {
+            const int64_t k = item(++it);
+            if (k < 0) return false;
+            I = decode_item(a, k);
+            if (I.n_entries > 0) return true;
+        }
+    }
+};
 
 // Bits of the 128 columns [k0, k0+128) that the BlockMask allows for query row qi
 // (attention.cpp:70-86; blocks outside the bitmap are disallowed).  Walks the few mask
@@ -167,39 +266,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* bar_base = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
     Bars bars;
     bars.q_full = bar_base;
-    bars.slot_full = bar_base + 1;
+    bars.q_empty = bars.q_full + 1;
+    bars.slot_full = bars.q_empty + 1;
     bars.slot_empty = bars.slot_full + kSlots;
     bars.s_full = bars.slot_empty + kSlots;
     bars.p_full = bars.s_full + 2;
-    bars.mma_done = bars.p_full + 2;
-    bars.drain = bars.mma_done + 1;
+    bars.o_done = bars.p_full + 2;
+    bars.drain = bars.o_done + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars.drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int bh = blockIdx.x;
-    const int pair = args.n_pairs - 1 - static_cast<int>(blockIdx.y);  // longest causal rows first
-    const int b = bh / args.heads_q;
-    const int h = bh - b * args.heads_q;
-    const int hk = h / (args.heads_q / args.heads_kv);
-    const int q00 = pair * 2 * kTileQ;        // first row of Q0
-    const int q01 = q00 + kTileQ;             // first row of Q1
-    const bool valid1 = q01 < args.m;
-    const int qend0 = min(args.m, q00 + kTileQ);
-    const int qend1 = valid1 ? min(args.m, q01 + kTileQ) : qend0;
-
-    int n_entries;
-    if (args.mode == kModeList) {
-        n_entries = args.tile_count[pair];
-    } else if (args.mode == kModeCausal) {
-        n_entries = min(args.n_kt, (qend1 + kTileK - 1) / kTileK);
-    } else {
-        n_entries = args.n_kt;
-    }
+    const ItemSchedule sched(args);
 
     if (threadIdx.x == 0) {
         ptx::mbar_init(bars.q_full, 1);
+        ptx::mbar_init(bars.q_empty, 1);
         for (int s = 0; s < kSlots; ++s) {
             ptx::mbar_init(&bars.slot_full[s], 1);
             ptx::mbar_init(&bars.slot_empty[s], 1);
@@ -207,8 +290,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) {
             ptx::mbar_init(&bars.s_full[i], 1);
             ptx::mbar_init(&bars.p_full[i], 128);
+            ptx::mbar_init(&bars.o_done[i], 1);
         }
-        ptx::mbar_init(bars.mma_done, 1);
         ptx::mbar_init(bars.drain, 1);
         *abort_flag = 0;
         ptx::fence_barrier_init();
@@ -223,344 +306,447 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == kWarpProducer) {
-        // ------------------------------------------------------------ TMA producer
-        if (lane == 0 && n_entries > 0) {
-            ptx::prefetch_tmap(&tmQ);
-            ptx::prefetch_tmap(&tmK);
-            ptx::prefetch_tmap(&tmV);
-            ptx::mbar_arrive_expect_tx(bars.q_full, (valid1 ? 2 : 1) * Cfg::kTileBytes);
-            for (int c = 0; c < Cfg::kChunks; ++c) {
-                ptx::tma_load_4d(sQ + c * kChunkBytes, &tmQ, bars.q_full, c * 64, q00, h, b);
-            }
-            if (valid1) {
-                for (int c = 0; c < Cfg::kChunks; ++c) {
-                    ptx::tma_load_4d(sQ + Cfg::kTileBytes + c * kChunkBytes, &tmQ, bars.q_full, c * 64, q01, h, b);
-                }
-            }
-            int issued = 0;  // ring uses issued so far (K and V tiles alternate)
-            for (int j = 0; j < n_entries && !*abort_flag; ++j) {
-                const int kt = static_cast<int>(kv_entry(args, pair, j, valid1, qend0, qend1) & 0xFFFFu);
-                for (int half = 0; half < 2; ++half) {
-                    const int t = 2 * j + half;
-                    const int s = t % kSlots;
-                    const int use = t / kSlots;
-                    if (use >= 1 && !ptx::mbar_wait(&bars.slot_empty[s], (use - 1) & 1, abort_flag, args.status,
-                                                    ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
+    if (warp >= kWarpProducer) {
+        // Warpgroup 2 (producer, MMA issuer, two idle warps) hands registers to the
+        // softmax warpgroups; all four of its warps execute this one instruction.
+        ptx::setmaxnreg_dec<kRegsCtrl>();
+        if (warp == kWarpProducer) {
+            // ------------------------------------------------------------ TMA producer
+            if (lane == 0) {
+                ptx::prefetch_tmap(&tmQ);
+                ptx::prefetch_tmap(&tmK);
+                ptx::prefetch_tmap(&tmV);
+                int issued = 0;  // ring uses so far, over all items (K and V tiles alternate)
+                int q_loads = 0;
+                bool ok = true;
+                for (int it = 0; ok && !*abort_flag; ++it) {
+                    const int64_t k = sched.item(it);
+                    if (k < 0) break;
+                    const Item I = decode_item(args, k);
+                    if (I.n_entries == 0) continue;
+                    // Q of this item replaces the previous item's once its last S MMAs have read it.
+                    if (q_loads > 0 && !(ok = ptx::mbar_wait(bars.q_empty, (q_loads - 1) & 1, abort_flag, args.status,
+                                                             ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)))
                         break;
-                    uint8_t* dst = sSlots + s * Cfg::kTileBytes;
-                    ptx::mbar_arrive_expect_tx(&bars.slot_full[s], Cfg::kTileBytes);
-                    const void* map = half == 0 ? static_cast<const void*>(&tmK) : static_cast<const void*>(&tmV);
+                    ptx::mbar_arrive_expect_tx(bars.q_full, (I.valid1 ? 2 : 1) * Cfg::kTileBytes);
                     for (int c = 0; c < Cfg::kChunks; ++c) {
-                        ptx::tma_load_4d(dst + c * kChunkBytes, map, &bars.slot_full[s], c * 64, kt * kTileK, hk, b);
+                        ptx::tma_load_4d(sQ + c * kChunkBytes, &tmQ, bars.q_full, c * 64, I.q00, I.h, I.b);
                     }
-                    ++issued;
+                    if (I.valid1) {
+                        for (int c = 0; c < Cfg::kChunks; ++c) {
+                            ptx::tma_load_4d(sQ + Cfg::kTileBytes + c * kChunkBytes, &tmQ, bars.q_full, c * 64, I.q01,
+                                             I.h, I.b);
+                        }
+                    }
+                    ++q_loads;
+                    for (int j = 0; ok && j < I.n_entries; ++j) {
+                        const int kt = static_cast<int>(kv_entry(args, I, j) & 0xFFFFu);
+                        for (int half = 0; half < 2; ++half) {
+                            const int t = issued;
+                            const int s = t % kSlots;
+                            const int use = t / kSlots;
+                            if (use >= 1 && !(ok = ptx::mbar_wait(&bars.slot_empty[s], (use - 1) & 1, abort_flag,
+                                                                  args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)))
+                                break;
+                            uint8_t* dst = sSlots + s * Cfg::kTileBytes;
+                            ptx::mbar_arrive_expect_tx(&bars.slot_full[s], Cfg::kTileBytes);
+                            const void* map = half == 0 ? static_cast<const void*>(&tmK) : static_cast<const void*>(&tmV);
+                            for (int c = 0; c < Cfg::kChunks; ++c) {
+                                ptx::tma_load_4d(dst + c * kChunkBytes, map, &bars.slot_full[s], c * 64, kt * kTileK,
+                                                 I.hk, I.b);
+                            }
+                            ++issued;
+                        }
+                    }
+                }
+                if (!ok || *abort_flag) {
+                    // Let copies already issued land before the CTA's shared memory is released.
+                    volatile int no_abort = 0;
+                    const int first = issued > kSlots ? issued - kSlots : 0;
+                    for (int t = first; t < issued; ++t) {
+                        ptx::mbar_wait(&bars.slot_full[t % kSlots], (t / kSlots) & 1, &no_abort, nullptr, 0,
+                                       kWaitLimitNs);
+                    }
+                    if (q_loads > 0) ptx::mbar_wait(bars.q_full, (q_loads - 1) & 1, &no_abort, nullptr, 0, kWaitLimitNs);
                 }
             }
-            if (*abort_flag) {
-                // Let copies already issued land before the CTA's shared memory is released.
-                volatile int no_abort = 0;
-                const int first = issued > kSlots ? issued - kSlots : 0;
-                for (int t = first; t < issued; ++t) {
-                    ptx::mbar_wait(&bars.slot_full[t % kSlots], (t / kSlots) & 1, &no_abort, nullptr, 0,
-                                   kWaitLimitNs);
-                }
-                ptx::mbar_wait(bars.q_full, 0, &no_abort, nullptr, 0, kWaitLimitNs);
-            }
-        }
-    } else if (warp == kWarpMma) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0 && n_entries > 0) {
-            constexpr uint32_t kIdescQK = ptx::make_idesc_bf16(128, 128, false);
-            constexpr uint32_t kIdescPV = ptx::make_idesc_bf16(128, D, true);
-            const uint64_t q_desc0 = ptx::make_sdesc_sw128(ptx::smem_u32(sQ), 16, 1024);
-            const uint64_t q_desc1 = ptx::make_sdesc_sw128(ptx::smem_u32(sQ + Cfg::kTileBytes), 16, 1024);
-            const uint64_t k_desc0 = ptx::make_sdesc_sw128(ptx::smem_u32(sSlots), 16, 1024);
-            const uint64_t v_desc0 = ptx::make_sdesc_sw128(ptx::smem_u32(sSlots), kChunkBytes, 1024);
-            constexpr uint64_t kSlotStep = Cfg::kTileBytes >> 4;  // descriptor units per ring slot
-            int pv_count[2] = {0, 0};
-            bool ok = true;
+        } else if (warp == kWarpMma) {
+            // ------------------------------------------------------------ MMA issuer
+            if (lane == 0) {
+                constexpr uint32_t kIdescQK = ptx::make_idesc_bf16(128, 128, false);
+                constexpr uint32_t kIdescPV = ptx::make_idesc_bf16(128, D, true);
+                constexpr uint32_t kDescHi = ptx::sdesc_sw128_hi(1024);
+                const uint32_t q_lo0 = ptx::sdesc_sw128_lo(ptx::smem_u32(sQ), 16);
+                const uint32_t q_lo1 = ptx::sdesc_sw128_lo(ptx::smem_u32(sQ + Cfg::kTileBytes), 16);
+                const uint32_t k_lo0 = ptx::sdesc_sw128_lo(ptx::smem_u32(sSlots), 16);
+                const uint32_t v_lo0 = ptx::sdesc_sw128_lo(ptx::smem_u32(sSlots), kChunkBytes);
+                constexpr uint32_t kSlotStep = Cfg::kTileBytes >> 4;  // descriptor units per ring slot
+                int pv_count[2] = {0, 0};     // P.V MMAs so far (parity of p_full)
+                bool acc[2] = {false, false};  // O_i already holds a P.V of the current item
+                int q_loads = 0;
+                bool ok = true;
 
-            // S_i = Q_i K^T (SS, M=128, N=128, K=D) into TMEM columns [128 i, 128 i + 128).
-            auto issue_s = [&](int i, int slot) {
-                const uint64_t qd = i == 0 ? q_desc0 : q_desc1;
-                const uint64_t kd = k_desc0 + static_cast<uint64_t>(slot) * kSlotStep;
+                // S_i = Q_i K^T (SS, M=128, N=128, K=D) into TMEM columns [128 i, 128 i + 128).
+                auto issue_s = [&](int i, int slot) {
+                    const uint32_t qd = i == 0 ? q_lo0 : q_lo1;
+                    const uint32_t kd = k_lo0 + static_cast<uint32_t>(slot) * kSlotStep;
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4);
-                    ptx::mma_bf16_ss(tmem + i * 128, qd + off, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
-                }
-                ptx::tc_commit(&bars.s_full[i]);
-            };
-            // O_i += P_i V (TS: P_i from TMEM, V MN-major from shared memory; M=128, N=D, K=128).
-            auto issue_pv = [&](int i, int slot) -> bool {
-                if (!ptx::mbar_wait(&bars.p_full[i], pv_count[i] & 1, abort_flag, args.status,
-                                    ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
-                    return false;
-                ptx::tc_fence_after();
-                const uint64_t vd = v_desc0 + static_cast<uint64_t>(slot) * kSlotStep;
-                const uint32_t first = pv_count[i] > 0 ? 1u : 0u;
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        const uint32_t off = static_cast<uint32_t>(((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4);
+                        ptx::mma_bf16_ss_lo(tmem + i * 128, qd + off, kd + off, kDescHi, kIdescQK, kk > 0 ? 1u : 0u);
+                    }
+                    ptx::tc_commit(&bars.s_full[i]);
+                };
+                // O_i += P_i V (TS: P_i from TMEM, V MN-major from shared memory; M=128, N=D, K=128).
+                auto issue_pv = [&](int i, int slot) -> bool {
+                    if (!ptx::mbar_wait(&bars.p_full[i], pv_count[i] & 1, abort_flag, args.status,
+                                        ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
+                        return false;
+                    ptx::tc_fence_after();
+                    const uint32_t vd = v_lo0 + static_cast<uint32_t>(slot) * kSlotStep;
+                    const uint32_t first = acc[i] ? 1u : 0u;
 #pragma unroll
-                for (int kk = 0; kk < kTileK / 16; ++kk) {
-                    ptx::mma_bf16_ts(tmem + Cfg::kTmemO + i * D, tmem + i * 128 + kk * 8,
-                                     vd + static_cast<uint64_t>(kk * (2048 >> 4)), kIdescPV, (first | kk) ? 1u : 0u);
-                }
-                ++pv_count[i];
-                return true;
-            };
-            auto wait_full = [&](int t) -> bool {
-                return ptx::mbar_wait(&bars.slot_full[t % kSlots], (t / kSlots) & 1, abort_flag, args.status,
-                                      ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
-            };
-
-            ok = ptx::mbar_wait(bars.q_full, 0, abort_flag, args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
-            uint32_t e = kv_entry(args, pair, 0, valid1, qend0, qend1);
-            if (ok) ok = wait_full(0);
-            if (ok) {
-                ptx::tc_fence_after();
-                if (e & kNeed0) issue_s(0, 0);
-                if (e & kNeed1) issue_s(1, 0);
-                ptx::tc_commit(&bars.slot_empty[0]);
-            }
-            for (int j = 0; ok && j < n_entries; ++j) {
-                const int tv = 2 * j + 1;  // V_j ring index
-                const int tk = 2 * j + 2;  // K_{j+1} ring index
-                const bool more = j + 1 < n_entries;
-                const uint32_t en = more ? kv_entry(args, pair, j + 1, valid1, qend0, qend1) : 0u;
-                if (!(ok = wait_full(tv))) break;
-                ptx::tc_fence_after();
-                if ((e & kNeed0) && !(ok = issue_pv(0, tv % kSlots))) break;
-                if (more) {
-                    if (!(ok = wait_full(tk))) break;
+                    for (int kk = 0; kk < kTileK / 16; ++kk) {
+                        ptx::mma_bf16_ts_lo(tmem + Cfg::kTmemO + i * D, tmem + i * 128 + kk * 8,
+                                            vd + static_cast<uint32_t>(kk * (2048 >> 4)), kDescHi, kIdescPV,
+                                            (first | kk) ? 1u : 0u);
+                    }
+                    acc[i] = true;
+                    ++pv_count[i];
+                    return true;
+                };
+                auto wait_full = [&](int t) -> bool {
+                    return ptx::mbar_wait(&bars.slot_full[t % kSlots], (t / kSlots) & 1, abort_flag, args.status,
+                                          ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+                };
+                // Q of the next item, then S_0/S_1 of its first KV tile (ring index tk).
+                auto start_item = [&](const Item& In, uint32_t en, int tk) -> bool {
+                    if (!ptx::mbar_wait(bars.q_full, q_loads & 1, abort_flag, args.status, ODF_ERR_DEVICE_TIMEOUT,
+                                        kWaitLimitNs))
+                        return false;
+                    ++q_loads;
+                    if (!wait_full(tk)) return false;
                     ptx::tc_fence_after();
                     if (en & kNeed0) issue_s(0, tk % kSlots);
-                }
-                if ((e & kNeed1) && !(ok = issue_pv(1, tv % kSlots))) break;
-                ptx::tc_commit(&bars.slot_empty[tv % kSlots]);
-                if (more) {
                     if (en & kNeed1) issue_s(1, tk % kSlots);
                     ptx::tc_commit(&bars.slot_empty[tk % kSlots]);
+                    if (In.n_entries == 1) ptx::tc_commit(bars.q_empty);
+                    return true;
+                };
+
+                int it = -1;
+                Item I;
+                const bool have = sched.next_nonempty(args, it, I);
+                uint32_t e = have ? kv_entry(args, I, 0) : 0u;
+                if (have) ok = start_item(I, e, 0);
+                for (int j = 0, g = 0; have && ok; ++g) {
+                    const int tv = 2 * g + 1;  // V of the current entry
+                    const int tk = 2 * g + 2;  // K of the next entry
+                    const bool last = j + 1 == I.n_entries;
+                    if (!(ok = wait_full(tv))) break;
+                    ptx::tc_fence_after();
+                    if (!last) {
+                        const uint32_t en = kv_entry(args, I, j + 1);
+                        if ((e & kNeed0) && !(ok = issue_pv(0, tv % kSlots))) break;
+                        if (!(ok = wait_full(tk))) break;
+                        ptx::tc_fence_after();
+                        if (en & kNeed0) issue_s(0, tk % kSlots);
+                        if ((e & kNeed1) && !(ok = issue_pv(1, tv % kSlots))) break;
+                        ptx::tc_commit(&bars.slot_empty[tv % kSlots]);
+                        if (en & kNeed1) issue_s(1, tk % kSlots);
+                        ptx::tc_commit(&bars.slot_empty[tk % kSlots]);
+                        if (j + 2 == I.n_entries) ptx::tc_commit(bars.q_empty);  // last S MMAs of the item issued
+                        e = en;
+                        ++j;
+                    } else {
+                        // last KV tile of the item: finish O_0 and O_1, then open the next item
+                        if ((e & kNeed0) && !(ok = issue_pv(0, tv % kSlots))) break;
+                        if (acc[0]) ptx::tc_commit(&bars.o_done[0]);
+                        if ((e & kNeed1) && !(ok = issue_pv(1, tv % kSlots))) break;
+                        ptx::tc_commit(&bars.slot_empty[tv % kSlots]);
+                        if (acc[1]) ptx::tc_commit(&bars.o_done[1]);
+                        acc[0] = acc[1] = false;
+                        if (!sched.next_nonempty(args, it, I)) break;
+                        e = kv_entry(args, I, 0);
+                        j = 0;
+                        if (!(ok = start_item(I, e, tk))) break;
+                    }
                 }
-                e = en;
+                if (!ok) {
+                    // Drain the MMAs already issued before the TMEM columns are freed.
+                    volatile int no_abort = 0;
+                    ptx::tc_commit(bars.drain);
+                    ptx::mbar_wait(bars.drain, 0, &no_abort, nullptr, 0, kWaitLimitNs);
+                }
             }
-            if (ok) {
-                ptx::tc_commit(bars.mma_done);
-            } else {
-                // Drain the MMAs already issued before the TMEM columns are freed.
-                volatile int no_abort = 0;
-                ptx::tc_commit(bars.drain);
-                ptx::mbar_wait(bars.drain, 0, &no_abort, nullptr, 0, kWaitLimitNs);
-            }
+        }
+        // ------------------------------------------------------------ teardown (control side)
+        ptx::tc_fence_before();
+        ptx::cta_barrier();
+        if (warp == kWarpProducer) {
+            ptx::tc_fence_after();
+            ptx::tmem_dealloc(tmem, kTmemCols);
         }
     } else {
         // ------------------------------------------------------------ softmax warps
+        ptx::setmaxnreg_inc<kRegsSoftmax>();
         const int qtile = warp >> 2;         // 0: Q0, 1: Q1
         const int wq = warp & 3;             // TMEM lane quarter
         const int row = wq * 32 + lane;      // 0..127 == TMEM lane
-        const int q0 = qtile == 0 ? q00 : q01;
-        const int qi = q0 + row;
         const uint32_t need_bit = qtile == 0 ? kNeed0 : kNeed1;
         const uint32_t bitmap_bit = qtile == 0 ? kBitmap0 : kBitmap1;
         const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
         const uint32_t s_addr = tmem + lane_off + qtile * 128;
         const uint32_t o_addr = tmem + lane_off + Cfg::kTmemO + qtile * D;
-        float m_run = -INFINITY;  // running (reference) max, log2 units
-        float l_run = 0.0f;       // running sum relative to m_run
-        float slope = 0.0f;
-        if (MOD & kModAlibi) {
-            slope = args.alibi_generated
-                        ? exp2f(-8.0f * static_cast<float>(h + 1) / static_cast<float>(args.heads_q))
-                        : args.alibi_slopes[h];
-        }
-        const float slope_log2 = slope * kLog2e;
+        // bit 0: parity of the next s_full wait, bit 1: of the next o_done wait,
+        // bit 2: the current item has fed O_i (at least one S_i tile processed)
+        uint32_t phases = 0;
         bool ok = true;
-        int cnt = 0;
 
-        for (int j = 0; j < n_entries; ++j) {
-            const uint32_t e = kv_entry(args, pair, j, valid1, qend0, qend1);
-            if (!(e & need_bit)) continue;
-            const int kt = static_cast<int>(e & 0xFFFFu);
-            const int k0 = kt * kTileK;
-            // Waits are per thread; the warp re-converges (and agrees) before the
-            // .sync.aligned TMEM accesses that follow.
-            const bool got = ptx::mbar_wait(&bars.s_full[qtile], cnt & 1, abort_flag, args.status,
-                                            ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
-            if (!__all_sync(0xffffffffu, got)) {
-                ok = false;
-                break;
-            }
-            ptx::tc_fence_after();
-            float s[128];
-            ptx::tmem_ld128(s_addr, s);
-            if (row == 0 && args.visits) {
-                args.visits[(static_cast<int64_t>(bh) * args.n_qt + (q0 / kTileQ)) * args.n_kt + kt] = 1;
-            }
+        RowItem* rec_w = reinterpret_cast<RowItem*>(smem + Cfg::kOffRows) + warp;
+        const volatile RowItem* rec = rec_w;
 
-            // score_mod: s*scale (+ ALiBi) (-> soft-cap), in log2 units (attention.cpp:619).
-            // Without a score_mod the scale is folded into the exponent below (raw scores).
-            const bool raw = (MOD == 0) && (args.scale_log2 > 0.0f);
-            if (MOD & kModSoftcap) {
-                const float base = static_cast<float>(k0 - qi);
-                const uint64_t scale2 = ptx::f32x2(args.scale);
-                const uint64_t slope2 = ptx::f32x2(slope);
-                const uint64_t sb2 = ptx::f32x2(slope * base);
-                const uint64_t k2 = ptx::f32x2(2.0f * kLog2e * args.inv_softcap);
-                const uint64_t cap_log2 = ptx::f32x2(args.softcap * kLog2e);
+        for (int it = 0; ok; ++it) {
+            const int64_t item = sched.item(it);
+            if (item < 0) break;
+            __syncwarp();  // every lane is done with the previous record
+            if (lane == 0) {
+                const Item I = decode_item(args, item);
+                RowItem r;
+                r.n_entries = I.n_entries;
+                r.pair = I.pair;
+                r.q0 = qtile == 0 ? I.q00 : I.q01;
+                const bool valid = qtile == 0 || I.valid1;
+                if (args.mode == kModeList) {
+                    r.n_iter = I.n_entries;
+                } else if (!valid) {
+                    r.n_iter = 0;
+                } else if (args.mode == kModeCausal) {  // tiles j with j * 128 < row end (as kv_entry)
+                    r.n_iter = min(I.n_entries, ((qtile == 0 ? I.qend0 : I.qend1) + kTileK - 1) / kTileK);
+                } else {
+                    r.n_iter = I.n_entries;
+                }
+                r.bh = I.bh;
+                r.b = I.b;
+                r.h = I.h;
+                r.slope = 0.0f;
+                if (MOD & kModAlibi) {
+                    r.slope = args.alibi_generated
+                                  ? exp2f(-8.0f * static_cast<float>(I.h + 1) / static_cast<float>(args.heads_q))
+                                  : args.alibi_slopes[I.h];
+                }
+                *rec_w = r;
+            }
+            __syncwarp();
+            float m_run = -INFINITY;  // running (reference) max, log2 units
+            float l_run = 0.0f;       // running sum relative to m_run
+            phases &= 3u;
+
+            const int n_iter = rec->n_iter;
+            for (int j = 0; j < n_iter; ++j) {
+                uint32_t e = static_cast<uint32_t>(j) | need_bit;
+                if (args.mode == kModeList) {
+                    e = __ldg(args.tile_list + static_cast<int64_t>(rec->pair) * args.n_kt + j);
+                    if (!(e & need_bit)) continue;
+                }
+                const int kt = static_cast<int>(e & 0xFFFFu);
+                const int k0 = kt * kTileK;
+                const int q0 = rec->q0;  // loaded ahead of the wait, which hides its latency
+                // Waits are per thread; the warp re-converges (and agrees) before the
+                // .sync.aligned TMEM accesses that follow.
+                const bool got = ptx::mbar_wait(&bars.s_full[qtile], phases & 1u, abort_flag, args.status,
+                                                ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+                if (!__all_sync(0xffffffffu, got)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const int qi = q0 + row;
+                float slope = 0.0f, slope_log2 = 0.0f;
+                if (MOD & kModAlibi) {
+                    slope = rec->slope;
+                    slope_log2 = slope * kLog2e;
+                }
+                float s[128];
+                ptx::tmem_ld128(s_addr, s);
+                if (row == 0 && args.visits) {
+                    args.visits[(static_cast<int64_t>(rec->bh) * args.n_qt + (q0 / kTileQ)) * args.n_kt + kt] = 1;
+                }
+
+                // score_mod: s*scale (+ ALiBi) (-> soft-cap), in log2 units (attention.cpp:619).
+                // Without a score_mod the scale is folded into the exponent below (raw scores).
+                const bool raw = (MOD == 0) && (args.scale_log2 > 0.0f);
+                if (MOD & kModSoftcap) {
+                    const float base = static_cast<float>(k0 - qi);
+                    const uint64_t scale2 = ptx::f32x2(args.scale);
+                    const uint64_t slope2 = ptx::f32x2(slope);
+                    const uint64_t sb2 = ptx::f32x2(slope * base);
+                    const uint64_t k2 = ptx::f32x2(2.0f * kLog2e * args.inv_softcap);
+                    const uint64_t cap_log2 = ptx::f32x2(args.softcap * kLog2e);
 #pragma unroll
-                for (int c = 0; c < 128; c += 2) {
-                    uint64_t x = ptx::f32x2(s[c], s[c + 1]);
-                    if (MOD & kModAlibi) {
-                        const uint64_t bias = ptx::ffma2(ptx::f32x2(static_cast<float>(c), static_cast<float>(c + 1)),
-                                                         slope2, sb2);
-                        x = ptx::ffma2(x, scale2, bias);
-                    } else {
-                        x = ptx::fmul2(x, scale2);
+                    for (int c = 0; c < 128; c += 2) {
+                        uint64_t x = ptx::f32x2(s[c], s[c + 1]);
+                        if (MOD & kModAlibi) {
+                            const uint64_t bias = ptx::ffma2(ptx::f32x2(static_cast<float>(c), static_cast<float>(c + 1)),
+                                                             slope2, sb2);
+                            x = ptx::ffma2(x, scale2, bias);
+                        } else {
+                            x = ptx::fmul2(x, scale2);
+                        }
+                        const uint64_t y = softcap2(x, k2, cap_log2);
+                        s[c] = ptx::lo_f32(y);
+                        s[c + 1] = ptx::hi_f32(y);
                     }
-                    const uint64_t y = softcap2(x, k2, cap_log2);
-                    s[c] = ptx::lo_f32(y);
-                    s[c + 1] = ptx::hi_f32(y);
-                }
-            } else if (MOD & kModAlibi) {
-                const float base = static_cast<float>(k0 - qi);
+                } else if (MOD & kModAlibi) {
+                    const float base = static_cast<float>(k0 - qi);
 #pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    s[c] = fmaf(s[c], args.scale_log2, slope_log2 * (base + static_cast<float>(c)));
-                }
-            } else if (!raw) {
+                    for (int c = 0; c < 128; ++c) {
+                        s[c] = fmaf(s[c], args.scale_log2, slope_log2 * (base + static_cast<float>(c)));
+                    }
+                } else if (!raw) {
 #pragma unroll
-                for (int c = 0; c < 128; ++c) s[c] *= args.scale_log2;
-            }
+                    for (int c = 0; c < 128; ++c) s[c] *= args.scale_log2;
+                }
 
-            // element mask on boundary tiles (attention.cpp:54-62, 608-617): column c of the
-            // tile survives iff c <= limit (causal kj <= qi, ragged kj < N) and, on tiles that
-            // cover a disallowed BlockMask block, its bit in the row's 128-bit allow mask.
-            const bool ragged = (k0 + kTileK > args.n);
-            const bool diag = args.causal && (min(args.n, k0 + kTileK) - 1 > q0);
-            const bool bitmap = (e & bitmap_bit) != 0;
-            if (ragged || diag || bitmap) {
-                int limit = args.n - 1 - k0;
-                if (args.causal) limit = min(limit, qi - k0);
-                const uint4 allow = bitmap ? row_allow_bits(args, qi, k0)
-                                           : make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+                // element mask on boundary tiles (attention.cpp:54-62, 608-617): column c of the
+                // tile survives iff c <= limit (causal kj <= qi, ragged kj < N) and, on tiles that
+                // cover a disallowed BlockMask block, its bit in the row's 128-bit allow mask.
+                const bool ragged = (k0 + kTileK > args.n);
+                const bool diag = args.causal && (min(args.n, k0 + kTileK) - 1 > q0);
+                const bool bitmap = (e & bitmap_bit) != 0;
+                if (ragged || diag || bitmap) {
+                    int limit = args.n - 1 - k0;
+                    if (args.causal) limit = min(limit, qi - k0);
+                    const uint4 allow = bitmap ? row_allow_bits(args, qi, k0)
+                                               : make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
 #pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    const uint32_t word = (c < 32) ? allow.x : (c < 64) ? allow.y : (c < 96) ? allow.z : allow.w;
-                    const bool keep = (c <= limit) && ((word >> (c & 31)) & 1u);
-                    s[c] = keep ? s[c] : -INFINITY;
+                    for (int c = 0; c < 128; ++c) {
+                        const uint32_t word = (c < 32) ? allow.x : (c < 64) ? allow.y : (c < 96) ? allow.z : allow.w;
+                        const bool keep = (c <= limit) && ((word >> (c & 31)) & 1u);
+                        s[c] = keep ? s[c] : -INFINITY;
+                    }
                 }
-            }
 
-            // online softmax (attention.cpp:628-644, 662-674) with tree reductions
-            float mx8[8];
+                // online softmax (attention.cpp:628-644, 662-674) with tree reductions
+                float mx8[8];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) mx8[t] = s[t];
+                for (int t = 0; t < 8; ++t) mx8[t] = s[t];
 #pragma unroll
-            for (int c = 8; c < 128; c += 2) mx8[(c >> 1) & 7] = ptx::fmax3(mx8[(c >> 1) & 7], s[c], s[c + 1]);
-            float tile_max = ptx::fmax3(ptx::fmax3(mx8[0], mx8[1], mx8[2]), ptx::fmax3(mx8[3], mx8[4], mx8[5]),
-                                        fmaxf(mx8[6], mx8[7]));
-            if (raw) tile_max *= args.scale_log2;
-            float alpha = 1.0f;
-            if (m_run == -INFINITY) {
-                m_run = tile_max;  // first valid tile of this row: O holds zeros so far
-            } else if (tile_max > m_run + kRescaleLog2) {
-                alpha = ptx::ex2(m_run - tile_max);
-                m_run = tile_max;
-            }
-            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            // P = 2^(x - m) on fp32 pairs; the bf16 pairs are packed in place into s[0..63]
-            // (element c/2 is written only after s[c] and s[c+1] were consumed).
-            uint64_t sum2[4] = {0, 0, 0, 0};
-            {
-                const uint64_t mul2 = ptx::f32x2(raw ? args.scale_log2 : 1.0f);
-                const uint64_t neg2 = ptx::f32x2(-m_use);
-#pragma unroll
-                for (int c = 0; c < 128; c += 2) {
-                    const uint64_t x = ptx::ffma2(ptx::f32x2(s[c], s[c + 1]), mul2, neg2);
-                    const float p0 = ptx::ex2(ptx::lo_f32(x));
-                    const float p1 = ptx::ex2(ptx::hi_f32(x));
-                    sum2[(c >> 1) & 3] = ptx::fadd2(sum2[(c >> 1) & 3], ptx::f32x2(p0, p1));
-                    s[c >> 1] = __uint_as_float(ptx::pack_bf16x2(p0, p1));
+                for (int c = 8; c < 128; c += 2) mx8[(c >> 1) & 7] = ptx::fmax3(mx8[(c >> 1) & 7], s[c], s[c + 1]);
+                float tile_max = ptx::fmax3(ptx::fmax3(mx8[0], mx8[1], mx8[2]), ptx::fmax3(mx8[3], mx8[4], mx8[5]),
+                                            fmaxf(mx8[6], mx8[7]));
+                if (raw) tile_max *= args.scale_log2;
+                float alpha = 1.0f;
+                if (m_run == -INFINITY) {
+                    m_run = tile_max;  // first valid tile of this row: O holds zeros so far
+                } else if (tile_max > m_run + kRescaleLog2) {
+                    alpha = ptx::ex2(m_run - tile_max);
+                    m_run = tile_max;
                 }
-            }
-            const uint64_t sum_all = ptx::fadd2(ptx::fadd2(sum2[0], sum2[1]), ptx::fadd2(sum2[2], sum2[3]));
-            l_run = l_run * alpha + (ptx::lo_f32(sum_all) + ptx::hi_f32(sum_all));
+                const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+                // P = 2^(x - m) on fp32 pairs; the bf16 pairs are packed in place into s[0..63]
+                // (element c/2 is written only after s[c] and s[c+1] were consumed).
+                uint64_t sum2[4] = {0, 0, 0, 0};
+                {
+                    const uint64_t mul2 = ptx::f32x2(raw ? args.scale_log2 : 1.0f);
+                    const uint64_t neg2 = ptx::f32x2(-m_use);
+#pragma unroll
+                    for (int c = 0; c < 128; c += 2) {
+                        const uint64_t x = ptx::ffma2(ptx::f32x2(s[c], s[c + 1]), mul2, neg2);
+                        const float p0 = ptx::ex2(ptx::lo_f32(x));
+                        const float p1 = ptx::ex2(ptx::hi_f32(x));
+                        sum2[(c >> 1) & 3] = ptx::fadd2(sum2[(c >> 1) & 3], ptx::f32x2(p0, p1));
+                        s[c >> 1] = __uint_as_float(ptx::pack_bf16x2(p0, p1));
+                    }
+                }
+                const uint64_t sum_all = ptx::fadd2(ptx::fadd2(sum2[0], sum2[1]), ptx::fadd2(sum2[2], sum2[3]));
+                l_run = l_run * alpha + (ptx::lo_f32(sum_all) + ptx::hi_f32(sum_all));
 
-            // correction: O_i *= alpha when the reference max moved (PV_i of the previous
-            // tile is complete: the commit that released S_i(j) covers every earlier MMA)
-            if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                // correction: O_i *= alpha when the reference max moved (PV_i of the previous
+                // tile is complete: the commit that released S_i(j) covers every earlier MMA)
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+                    for (int c = 0; c < D / 32; ++c) {
+                        float o[32];
+                        ptx::tmem_ld32(o_addr + c * 32, o);
+#pragma unroll
+                        for (int t = 0; t < 32; ++t) o[t] *= alpha;
+                        ptx::tmem_st32_nowait(o_addr + c * 32, reinterpret_cast<const uint32_t*>(o));
+                    }
+                }
+                // P_i over the first 64 columns of S_i, the A operand of PV_i
+                ptx::tmem_st64_nowait(s_addr, reinterpret_cast<const uint32_t*>(s));
+                ptx::tmem_st_wait();
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&bars.p_full[qtile]);
+                phases = (phases ^ 1u) | 4u;
+            }
+            if (!ok) break;
+
+            // ---------------------------------------------------------- epilogue
+            // O_i is final once the item's last P.V has completed; the next item's first P.V
+            // (which overwrites O_i) waits for this thread's next p_full arrival.
+            const bool fed = (phases & 4u) != 0;
+            if (fed) {
+                ok = ptx::mbar_wait(&bars.o_done[qtile], (phases >> 1) & 1u, abort_flag, args.status,
+                                    ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+                phases ^= 2u;
+                ptx::tc_fence_after();
+            }
+            ok = __all_sync(0xffffffffu, ok);
+            if (ok) {
+                const int b = rec->b;
+                const int h = rec->h;
+                const int qi = rec->q0 + row;
+                const bool valid_row = qi < args.m;
+                const float inv_l = (l_run > 0.0f) ? (1.0f / l_run) : 0.0f;
+                const int64_t orow = static_cast<int64_t>(b) * args.o_stride_b +
+                                     static_cast<int64_t>(h) * args.o_stride_h +
+                                     static_cast<int64_t>(qi) * args.o_stride_t;
 #pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
                     float o[32];
-                    ptx::tmem_ld32(o_addr + c * 32, o);
-#pragma unroll
-                    for (int t = 0; t < 32; ++t) o[t] *= alpha;
-                    ptx::tmem_st32_nowait(o_addr + c * 32, reinterpret_cast<const uint32_t*>(o));
-                }
-            }
-            // P_i over the first 64 columns of S_i, the A operand of PV_i
-            ptx::tmem_st64_nowait(s_addr, reinterpret_cast<const uint32_t*>(s));
-            ptx::tmem_st_wait();
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(&bars.p_full[qtile]);
-            ++cnt;
-        }
-
-        // ------------------------------------------------------------ epilogue
-        if (ok && cnt > 0) {
-            ok = ptx::mbar_wait(bars.mma_done, 0, abort_flag, args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
-            ptx::tc_fence_after();
-        }
-        ok = __all_sync(0xffffffffu, ok);
-        if (ok) {
-            const bool valid_row = qi < args.m;
-            const float inv_l = (l_run > 0.0f) ? (1.0f / l_run) : 0.0f;
-            const int64_t orow = static_cast<int64_t>(b) * args.o_stride_b + static_cast<int64_t>(h) * args.o_stride_h +
-                                 static_cast<int64_t>(qi) * args.o_stride_t;
-#pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
-                float o[32];
-                if (cnt > 0) {
-                    ptx::tmem_ld32(o_addr + c * 32, o);
-                } else {
-#pragma unroll
-                    for (int t = 0; t < 32; ++t) o[t] = 0.0f;
-                }
-                if (valid_row) {
-                    if (args.o_bf16) {
-                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(args.o) + orow + c * 32);
-#pragma unroll
-                        for (int v = 0; v < 4; ++v) {
-                            uint4 w;
-                            w.x = ptx::pack_bf16x2(o[8 * v + 0] * inv_l, o[8 * v + 1] * inv_l);
-                            w.y = ptx::pack_bf16x2(o[8 * v + 2] * inv_l, o[8 * v + 3] * inv_l);
-                            w.z = ptx::pack_bf16x2(o[8 * v + 4] * inv_l, o[8 * v + 5] * inv_l);
-                            w.w = ptx::pack_bf16x2(o[8 * v + 6] * inv_l, o[8 * v + 7] * inv_l);
-                            dst[v] = w;
-                        }
+                    if (fed) {
+                        ptx::tmem_ld32(o_addr + c * 32, o);
                     } else {
-                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(args.o) + orow + c * 32);
 #pragma unroll
-                        for (int v = 0; v < 8; ++v) {
-                            dst[v] = make_float4(o[4 * v + 0] * inv_l, o[4 * v + 1] * inv_l, o[4 * v + 2] * inv_l,
-                                                 o[4 * v + 3] * inv_l);
+                        for (int t = 0; t < 32; ++t) o[t] = 0.0f;
+                    }
+                    if (valid_row) {
+                        if (args.o_bf16) {
+                            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(args.o) + orow + c * 32);
+#pragma unroll
+                            for (int v = 0; v < 4; ++v) {
+                                uint4 w;
+                                w.x = ptx::pack_bf16x2(o[8 * v + 0] * inv_l, o[8 * v + 1] * inv_l);
+                                w.y = ptx::pack_bf16x2(o[8 * v + 2] * inv_l, o[8 * v + 3] * inv_l);
+                                w.z = ptx::pack_bf16x2(o[8 * v + 4] * inv_l, o[8 * v + 5] * inv_l);
+                                w.w = ptx::pack_bf16x2(o[8 * v + 6] * inv_l, o[8 * v + 7] * inv_l);
+                                dst[v] = w;
+                            }
+                        } else {
+                            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(args.o) + orow + c * 32);
+#pragma unroll
+                            for (int v = 0; v < 8; ++v) {
+                                dst[v] = make_float4(o[4 * v + 0] * inv_l, o[4 * v + 1] * inv_l, o[4 * v + 2] * inv_l,
+                                                     o[4 * v + 3] * inv_l);
+                            }
                         }
                     }
                 }
-            }
-            if (valid_row && args.lse) {
-                const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-                args.lse[static_cast<int64_t>(bh) * args.m + qi] =
-                    (l_run > 0.0f) ? (m_use + log2f(l_run)) * kLn2 : -INFINITY;
+                if (valid_row && args.lse) {
+                    const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+                    args.lse[static_cast<int64_t>(rec->bh) * args.m + qi] =
+                        (l_run > 0.0f) ? (m_use + log2f(l_run)) * kLn2 : -INFINITY;
+                }
             }
         }
-    }
 
-    // ---------------------------------------------------------------- teardown
-    ptx::tc_fence_before();
-    __syncthreads();
-    if (warp == kWarpProducer) {
-        ptx::tc_fence_after();
-        ptx::tmem_dealloc(tmem, kTmemCols);
+        // ------------------------------------------------------------ teardown (softmax side)
+        // Each role ends with its own copy of the CTA barrier, so the two register budgets
+        // never meet in common code.
+        ptx::tc_fence_before();
+        ptx::cta_barrier();
     }
 }
 
@@ -664,15 +850,25 @@ struct DeviceState {
     bool ready = false;
     int status_code = ODF_OK;
     int* status_ptr = nullptr;
+    int sm_count = 0;
 };
 constexpr int kMaxDevices = 64;
 DeviceState g_devices[kMaxDevices];
 std::mutex g_device_mutex;
 
+// Sets the shared-memory limit and checks that the kernel was compiled with the register
+// count the setmaxnreg split assumes: with fewer registers at launch the softmax warps'
+// increase could never be granted, so such a build is refused instead of launched.
 template <int D, int MOD>
-cudaError_t set_kernel_attrs() {
-    return cudaFuncSetAttribute(flash_fwd_kernel<D, MOD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                Config<D>::kSmemBytes);
+cudaError_t set_kernel_attrs(bool* regs_ok) {
+    cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<D, MOD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Config<D>::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, flash_fwd_kernel<D, MOD>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < kThreads) *regs_ok = false;
+    return cudaSuccess;
 }
 
 CUresult encode_bf16_4d(CUtensorMap* map, const void* ptr, int64_t feat, int64_t tokens, int64_t heads,
@@ -749,14 +945,20 @@ int ensure_device_ready(int device, const char** err) {
         return ODF_ERR_CUDA;
     }
     cudaError_t e = cudaSuccess;
-    if (e == cudaSuccess) e = set_kernel_attrs<64, 0>();
-    if (e == cudaSuccess) e = set_kernel_attrs<64, 1>();
-    if (e == cudaSuccess) e = set_kernel_attrs<64, 2>();
-    if (e == cudaSuccess) e = set_kernel_attrs<64, 3>();
-    if (e == cudaSuccess) e = set_kernel_attrs<128, 0>();
-    if (e == cudaSuccess) e = set_kernel_attrs<128, 1>();
-    if (e == cudaSuccess) e = set_kernel_attrs<128, 2>();
-    if (e == cudaSuccess) e = set_kernel_attrs<128, 3>();
+    bool regs_ok = true;
+    if (e == cudaSuccess) e = set_kernel_attrs<64, 0>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<64, 1>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<64, 2>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<64, 3>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<128, 0>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<128, 1>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<128, 2>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<128, 3>(&regs_ok);
+    if (e == cudaSuccess && !regs_ok) {
+        st.status_code = ODF_ERR_UNSUPPORTED;
+        *err = "flash kernel built with an unexpected register count (the warp register split needs 168)";
+        return ODF_ERR_UNSUPPORTED;
+    }
     void* sp = nullptr;
     if (e == cudaSuccess) e = cudaGetSymbolAddress(&sp, g_device_status);
     if (e != cudaSuccess) {
@@ -764,6 +966,7 @@ int ensure_device_ready(int device, const char** err) {
         return ODF_ERR_CUDA;
     }
     st.status_ptr = static_cast<int*>(sp);
+    st.sm_count = prop.multiProcessorCount;
     st.ready = true;
     return ODF_OK;
 }
@@ -829,7 +1032,14 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
         a.tile_count = count;
     }
     const int mod = (L.has_alibi ? kModAlibi : 0) | (L.has_softcap ? kModSoftcap : 0);
-    const dim3 grid(static_cast<unsigned>(a.batch * a.heads_q), static_cast<unsigned>(a.n_pairs), 1);
+    // persistent grid: one CTA per SM (the kernel's shared memory allows one), at most one per item
+    const int64_t n_items = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;
+    int sm_count = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_device_mutex);
+        sm_count = g_devices[device].sm_count;
+    }
+    const dim3 grid(static_cast<unsigned>(n_items < sm_count ? n_items : sm_count), 1, 1);
     cudaError_t e = (L.head_dim == 64) ? launch_d<64>(tq, tk, tv, a, mod, grid, stream)
                                        : launch_d<128>(tq, tk, tv, a, mod, grid, stream);
     if (e != cudaSuccess) {
