@@ -73,7 +73,8 @@ constexpr float kLn2 = 0.6931471805599453f;
 // (log2 units), so P stays below 2^8 and O is rescaled rarely.
 constexpr float kRescaleLog2 = 8.0f;
 
-enum ModFlags { kModAlibi = 1, kModSoftcap = 2 };
+// Score-mod variants: ALiBi and the same-shape bias are exclusive (one BiasKind per call).
+enum ModFlags { kModAlibi = 1, kModSoftcap = 2, kModBias = 4 };
 
 template <int D>
 struct Config {
@@ -84,7 +85,7 @@ struct Config {
     static constexpr uint32_t kOffBar = kOffSlots + kSlots * kTileBytes;
     static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 1;
     static constexpr uint32_t kOffRows = kOffBar + kNumBars * 8 + 16;  // after the barriers, TMEM slot, abort flag
-    static constexpr uint32_t kSmemBytes = kOffRows + 8 * 32 + 1024;     // + alignment slack
+    static constexpr uint32_t kSmemBytes = kOffRows + 8 * 40 + 1024;     // + alignment slack
     static constexpr uint32_t kTmemO = 256;
 };
 
@@ -108,9 +109,10 @@ struct RowItem {
     int q0;         // first row of this warp's query tile
     int n_iter;     // list mode: n_entries; dense/causal: the KV tiles this query tile needs (0..n_iter-1)
     int bh, b, h;
-    float slope;    // ALiBi slope of head h
+    float slope;       // ALiBi slope of head h
+    int64_t bias_off;  // same-shape bias: element offset of this (batch, head)'s plane
 };
-static_assert(sizeof(RowItem) == 32, "RowItem layout");
+static_assert(sizeof(RowItem) == 40, "RowItem layout");
 
 // KV tile j of this query-tile pair: kv index in the low 16 bits, kNeed*/kBitmap* flags above.
 __device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, int pair, int j, bool valid1, int qend0, int qend1) {
@@ -530,6 +532,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 r.b = I.b;
                 r.h = I.h;
                 r.slope = 0.0f;
+                r.bias_off = (MOD & kModBias) ? static_cast<int64_t>(I.b) * args.bias_s0 +
+                                                    static_cast<int64_t>(I.h) * args.bias_s1
+                                              : 0;
                 if (MOD & kModAlibi) {
                     r.slope = args.alibi_generated
                                   ? exp2f(-8.0f * static_cast<float>(I.h + 1) / static_cast<float>(args.heads_q))
@@ -573,9 +578,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                     args.visits[(static_cast<int64_t>(rec->bh) * args.n_qt + (q0 / kTileQ)) * args.n_kt + kt] = 1;
                 }
 
-                // score_mod: s*scale (+ ALiBi) (-> soft-cap), in log2 units (attention.cpp:619).
-                // Without a score_mod the scale is folded into the exponent below (raw scores).
+                // score_mod: s*scale (+ ALiBi or bias tensor) (-> soft-cap), in log2 units
+                // (attention.cpp:619).  Without a score_mod the scale is folded into the exponent
+                // below (raw scores).
                 const bool raw = (MOD == 0) && (args.scale_log2 > 0.0f);
+                if (MOD & kModBias) {
+                    // same-shape additive bias (qk_score_tile.cpp:28-47): s*scale + bias(qi, kj) in
+                    // the units of the next step (natural before a soft-cap, log2 otherwise).
+                    // Columns at or beyond N, and rows beyond M, are not read (masked or unused).
+                    const float mul = (MOD & kModSoftcap) ? args.scale : args.scale_log2;
+                    const float bmul = (MOD & kModSoftcap) ? 1.0f : kLog2e;
+                    const int ncols = (qi < args.m) ? min(kTileK, args.n - k0) : 0;
+                    const float* brow = args.bias + rec->bias_off + static_cast<int64_t>(qi) * args.bias_s2 +
+                                        static_cast<int64_t>(k0) * args.bias_s3;
+                    if (ncols == kTileK && args.bias_s3 == 1 && (reinterpret_cast<uintptr_t>(brow) & 15u) == 0) {
+                        const float4* b4 = reinterpret_cast<const float4*>(brow);
+#pragma unroll
+                        for (int c4 = 0; c4 < kTileK / 4; ++c4) {
+                            const float4 bv = __ldg(b4 + c4);
+                            s[4 * c4 + 0] = fmaf(s[4 * c4 + 0], mul, bv.x * bmul);
+                            s[4 * c4 + 1] = fmaf(s[4 * c4 + 1], mul, bv.y * bmul);
+                            s[4 * c4 + 2] = fmaf(s[4 * c4 + 2], mul, bv.z * bmul);
+                            s[4 * c4 + 3] = fmaf(s[4 * c4 + 3], mul, bv.w * bmul);
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < kTileK; ++c) {
+                            const float bv = c < ncols ? __ldg(brow + static_cast<int64_t>(c) * args.bias_s3) : 0.0f;
+                            s[c] = fmaf(s[c], mul, bv * bmul);
+                        }
+                    }
+                    // start bringing this row's next tile into L2 while the rest of the tile runs
+                    if (ncols == kTileK && args.bias_s3 == 1 && k0 + 2 * kTileK <= args.n) {
+#pragma unroll
+                        for (int l = 0; l < 4; ++l) ptx::prefetch_l2(brow + kTileK + 32 * l);
+                    }
+                }
                 if (MOD & kModSoftcap) {
                     const float base = static_cast<float>(k0 - qi);
                     const uint64_t scale2 = ptx::f32x2(args.scale);
@@ -590,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint64_t bias = ptx::ffma2(ptx::f32x2(static_cast<float>(c), static_cast<float>(c + 1)),
                                                              slope2, sb2);
                             x = ptx::ffma2(x, scale2, bias);
-                        } else {
+                        } else if (!(MOD & kModBias)) {  // the bias pass already scaled
                             x = ptx::fmul2(x, scale2);
                         }
                         const uint64_t y = softcap2(x, k2, cap_log2);
@@ -603,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int c = 0; c < 128; ++c) {
                         s[c] = fmaf(s[c], args.scale_log2, slope_log2 * (base + static_cast<float>(c)));
                     }
-                } else if (!raw) {
+                } else if (!raw && !(MOD & kModBias)) {
 #pragma unroll
                     for (int c = 0; c < 128; ++c) s[c] *= args.scale_log2;
                 }
@@ -893,7 +931,9 @@ cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
         case 0: flash_fwd_kernel<D, 0><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a); break;
         case 1: flash_fwd_kernel<D, 1><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a); break;
         case 2: flash_fwd_kernel<D, 2><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a); break;
-        default: flash_fwd_kernel<D, 3><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a); break;
+        case 3: flash_fwd_kernel<D, 3><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a); break;
+        case 4: flash_fwd_kernel<D, 4><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a); break;
+        default: flash_fwd_kernel<D, 6><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a); break;
     }
     return cudaGetLastError();
 }
@@ -950,10 +990,14 @@ int ensure_device_ready(int device, const char** err) {
     if (e == cudaSuccess) e = set_kernel_attrs<64, 1>(&regs_ok);
     if (e == cudaSuccess) e = set_kernel_attrs<64, 2>(&regs_ok);
     if (e == cudaSuccess) e = set_kernel_attrs<64, 3>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<64, 4>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<64, 6>(&regs_ok);
     if (e == cudaSuccess) e = set_kernel_attrs<128, 0>(&regs_ok);
     if (e == cudaSuccess) e = set_kernel_attrs<128, 1>(&regs_ok);
     if (e == cudaSuccess) e = set_kernel_attrs<128, 2>(&regs_ok);
     if (e == cudaSuccess) e = set_kernel_attrs<128, 3>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<128, 4>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<128, 6>(&regs_ok);
     if (e == cudaSuccess && !regs_ok) {
         st.status_code = ODF_ERR_UNSUPPORTED;
         *err = "flash kernel built with an unexpected register count (the warp register split needs 168)";
@@ -1031,7 +1075,7 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
         a.tile_list = list;
         a.tile_count = count;
     }
-    const int mod = (L.has_alibi ? kModAlibi : 0) | (L.has_softcap ? kModSoftcap : 0);
+    const int mod = (L.has_alibi ? kModAlibi : 0) | (L.has_softcap ? kModSoftcap : 0) | (L.has_bias ? kModBias : 0);
     // persistent grid: one CTA per SM (the kernel's shared memory allows one), at most one per item
     const int64_t n_items = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;
     int sm_count = 0;

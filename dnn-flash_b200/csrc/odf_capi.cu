@@ -25,6 +25,7 @@ int fail(int code, const std::string& msg) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 
 // Fills contiguous [B, H, T, D] strides when all three are zero.
 void resolve_strides(const int64_t in[3], int64_t heads, int64_t tokens, int64_t feat, int64_t out[3]) {
@@ -41,6 +42,7 @@ void resolve_strides(const int64_t in[3], int64_t heads, int64_t tokens, int64_t
 
 struct Resolved {
     int64_t qs[3], ks[3], vs[3], os[3];
+    int64_t bs[4];  // same-shape bias element strides (all-zero input = contiguous [B, Hq, M, N])
     int32_t n_qt, n_kt;
 };
 
@@ -72,8 +74,26 @@ int validate(const odf_fwd_params* p, bool host, Resolved* r) {
     if (!std::isfinite(p->scale)) return fail(ODF_ERR_INVALID_ARG, "scale must be finite");
     if (!(p->softcap >= 0.0f) || !std::isfinite(p->softcap))
         return fail(ODF_ERR_INVALID_ARG, "softcap must be finite and >= 0");
-    if (p->bias_kind != ODF_BIAS_NONE && p->bias_kind != ODF_BIAS_ALIBI)
-        return fail(ODF_ERR_UNSUPPORTED, "only BiasKind::None and BiasKind::AlibiGenerated run on the GPU");
+    if (p->bias_kind != ODF_BIAS_NONE && p->bias_kind != ODF_BIAS_ALIBI && p->bias_kind != ODF_BIAS_SAME_SHAPE)
+        return fail(ODF_ERR_UNSUPPORTED,
+                    "only BiasKind::None, SameShapeTile and AlibiGenerated run on the GPU");
+    if (p->bias_kind == ODF_BIAS_SAME_SHAPE) {
+        if (p->bias == nullptr) return fail(ODF_ERR_INVALID_ARG, "BiasKind::SameShapeTile needs a bias tensor");
+        for (int i = 0; i < 4; ++i)
+            if (p->bias_strides[i] < 0) return fail(ODF_ERR_INVALID_ARG, "bias strides must be >= 0");
+        if (!aligned4(p->bias)) return fail(ODF_ERR_INVALID_ARG, "the bias tensor must be 4-byte aligned");
+        const int64_t* s = p->bias_strides;
+        if (s[0] == 0 && s[1] == 0 && s[2] == 0 && s[3] == 0) {
+            r->bs[0] = p->heads_q * p->seqlen_q * p->seqlen_k;
+            r->bs[1] = p->seqlen_q * p->seqlen_k;
+            r->bs[2] = p->seqlen_k;
+            r->bs[3] = 1;
+        } else {
+            for (int i = 0; i < 4; ++i) r->bs[i] = s[i];
+        }
+    } else {
+        for (int i = 0; i < 4; ++i) r->bs[i] = 0;
+    }
     if (p->bias_kind == ODF_BIAS_ALIBI && p->alibi_slopes != nullptr && p->heads_q > ODF_MAX_EXPLICIT_SLOPES)
         return fail(ODF_ERR_UNSUPPORTED, "explicit ALiBi slopes are limited to 256 heads (use generated slopes)");
     if (p->block_mask != nullptr &&
@@ -122,6 +142,7 @@ odf::FwdLaunch make_launch(const odf_fwd_params* p, const Resolved& r) {
     L.head_dim = static_cast<int32_t>(p->head_dim);
     L.has_alibi = p->bias_kind == ODF_BIAS_ALIBI;
     L.has_softcap = p->softcap > 0.0f;
+    L.has_bias = p->bias_kind == ODF_BIAS_SAME_SHAPE;
     L.workspace = p->workspace;
     L.workspace_bytes = p->workspace_bytes;
     odf::FwdArgs& a = L.args;
@@ -150,6 +171,13 @@ odf::FwdLaunch make_launch(const odf_fwd_params* p, const Resolved& r) {
     a.mask_qblocks = static_cast<int32_t>(std::min<int64_t>(p->mask_qblocks, 0x7fffffff));
     a.mask_kblocks = static_cast<int32_t>(std::min<int64_t>(p->mask_kblocks, 0x7fffffff));
     a.visits = p->tile_visits;
+    if (p->bias_kind == ODF_BIAS_SAME_SHAPE) {
+        a.bias = p->bias;
+        a.bias_s0 = r.bs[0];
+        a.bias_s1 = r.bs[1];
+        a.bias_s2 = r.bs[2];
+        a.bias_s3 = r.bs[3];
+    }
     // Generated slopes are evaluated here on the host (for up to 256 heads) so that the
     // device entry and the chunked host entry use bit-identical values.
     a.alibi_generated = 0;
@@ -298,6 +326,30 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
         if (ws_bytes && (e = pool.reserve(slot, 6, ws_bytes, &dws)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+        // Same-shape bias: the footprint of each (batch, q-head) plane of this chunk, copied to a
+        // device staging buffer with the row/key strides kept (one plane when the bias is
+        // broadcast over batch and heads).
+        const float* dbias = nullptr;
+        int64_t bias_plane = 0;
+        if (p->bias_kind == ODF_BIAS_SAME_SHAPE) {
+            const int64_t* bs = r.bs;
+            const int64_t foot = (M - 1) * bs[2] + (N - 1) * bs[3] + 1;
+            const bool shared = bs[0] == 0 && bs[1] == 0;
+            const int64_t planes = shared ? 1 : cu * G;
+            bias_plane = shared ? 0 : (foot + 3) / 4 * 4;
+            void* db = nullptr;
+            if ((e = pool.reserve(slot, 7, static_cast<size_t>(shared ? foot : planes * bias_plane) * sizeof(float),
+                                  &db)) != cudaSuccess)
+                return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+            for (int64_t j = 0; j < planes && e == cudaSuccess; ++j) {
+                const int64_t gh = u0 * G + j;  // global (batch, q-head) index of this plane
+                const int64_t b = gh / p->heads_q, h = gh % p->heads_q;
+                e = cudaMemcpyAsync(static_cast<float*>(db) + j * bias_plane, p->bias + b * bs[0] + h * bs[1],
+                                    static_cast<size_t>(foot) * sizeof(float), cudaMemcpyHostToDevice, st);
+            }
+            if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+            dbias = static_cast<const float*>(db);
+        }
 
         const char* hq = static_cast<const char*>(p->q) + u0 * q_unit * in_es;
         const char* hk = static_cast<const char*>(p->k) + u0 * kv_unit * in_es;
@@ -330,6 +382,13 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         sub.workspace = dws;
         sub.workspace_bytes = ws_bytes;
         sub.tile_visits = nullptr;
+        if (dbias) {
+            sub.bias = dbias;
+            sub.bias_strides[0] = 0;  // the sub-launch has batch 1
+            sub.bias_strides[1] = bias_plane;
+            sub.bias_strides[2] = r.bs[2];
+            sub.bias_strides[3] = r.bs[3];  // never all four zero: r.bs came from a non-zero or contiguous set
+        }
         // ALiBi slopes are per q-head: shift to this chunk's heads (units never straddle a batch row
         // of heads when heads are re-based, so slopes are indexed by head within the batch).
         std::vector<float> slopes;

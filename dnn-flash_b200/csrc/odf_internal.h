@@ -49,6 +49,8 @@ struct FwdArgs {
     int* status;
     int32_t alibi_generated;    // slopes = 2^(-8 (h+1) / heads_q)
     float alibi_slopes[ODF_MAX_EXPLICIT_SLOPES];
+    const float* bias;          // same-shape additive bias, element strides below (0 = broadcast)
+    int64_t bias_s0, bias_s1, bias_s2, bias_s3;
 };
 
 // Validated, resolved launch request (device pointers only).
@@ -60,6 +62,7 @@ struct FwdLaunch {
     int32_t head_dim;
     int32_t has_alibi;
     int32_t has_softcap;
+    int32_t has_bias;
     FwdArgs args;
     void* workspace;
     size_t workspace_bytes;

@@ -162,9 +162,10 @@ void run_forward(const float* q, const float* k, const float* v, float* out, con
     if (opt.score_bias) {
         throw std::runtime_error(
             "GPU attention: AttentionOptions::score_bias is a host functor and cannot run on the device; "
-            "use bias_kind = BiasKind::AlibiGenerated");
+            "use bias_kind = BiasKind::AlibiGenerated or BiasKind::SameShapeTile");
     }
-    if (opt.bias_kind != BiasKind::None && opt.bias_kind != BiasKind::AlibiGenerated) {
+    if (opt.bias_kind != BiasKind::None && opt.bias_kind != BiasKind::AlibiGenerated &&
+        opt.bias_kind != BiasKind::SameShapeTile) {
         throw std::runtime_error(std::string("GPU attention: bias kind ") + to_string(opt.bias_kind) +
                                  " is not supported on the device");
     }
@@ -184,8 +185,15 @@ void run_forward(const float* q, const float* k, const float* v, float* out, con
     p.value_dim = static_cast<int64_t>(pb.dv);
     p.scale = opt.scale;
     p.causal = opt.causal ? 1 : 0;
-    p.bias_kind = opt.bias_kind == BiasKind::AlibiGenerated ? ODF_BIAS_ALIBI : ODF_BIAS_NONE;
+    p.bias_kind = opt.bias_kind == BiasKind::AlibiGenerated ? ODF_BIAS_ALIBI
+                  : opt.bias_kind == BiasKind::SameShapeTile ? ODF_BIAS_SAME_SHAPE
+                                                             : ODF_BIAS_NONE;
     p.alibi_slopes = opt.alibi_slopes;
+    if (opt.bias_kind == BiasKind::SameShapeTile) {
+        if (opt.bias == nullptr) throw std::invalid_argument("BiasKind::SameShapeTile needs AttentionOptions::bias");
+        p.bias = opt.bias;
+        for (int i = 0; i < 4; ++i) p.bias_strides[i] = opt.bias_strides[i];
+    }
     p.softcap = opt.softcap;
     p.lse = opt.lse;
     if (opt.block_mask) {
@@ -198,6 +206,9 @@ void run_forward(const float* q, const float* k, const float* v, float* out, con
     const bool dq = on_device(q), dk = on_device(k), dvp = on_device(v), dout = on_device(out);
     if (!(dq == dk && dk == dvp && dvp == dout)) {
         throw std::invalid_argument("q, k, v and output must all be host memory or all be device memory");
+    }
+    if (p.bias != nullptr && on_device(p.bias) != dq) {
+        throw std::invalid_argument("the bias tensor must be in the same memory kind as q, k, v");
     }
     if (!dq) {
         // Host buffers: streamed through the device by the host entry.

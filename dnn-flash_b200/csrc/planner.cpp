@@ -167,7 +167,9 @@ ScoreModPlan make_sm100_score_mod_plan(ScoreModKind requested_kind, DataType dty
         plan.signature = unsupported_signature(plan.fallback_reason);
         return plan;
     }
-    if (plan.has_bias && requested_bias_kind != BiasKind::AlibiGenerated) {
+    if (plan.has_bias && requested_bias_kind != BiasKind::AlibiGenerated &&
+        requested_bias_kind != BiasKind::SameShapeTile) {
+        // row/column broadcasts are SameShapeTile tensors with zero strides on this path
         const bool broadcast =
             requested_bias_kind == BiasKind::BroadcastRow || requested_bias_kind == BiasKind::BroadcastCol;
         plan.lowering_status = LoweringStatus::Unsupported;

@@ -28,6 +28,7 @@ ODF_ERR_NO_DEVICE = 5
 ODF_DTYPE_F32 = 0
 ODF_DTYPE_BF16 = 1
 ODF_BIAS_NONE = 0
+ODF_BIAS_SAME_SHAPE = 1
 ODF_BIAS_ALIBI = 4
 TILE_Q = 128
 TILE_K = 128
@@ -47,6 +48,7 @@ class FwdParams(C.Structure):
         ("bias_kind", C.c_int32), ("alibi_slopes", C.c_void_p), ("softcap", C.c_float),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
         ("tile_visits", C.c_void_p),
+        ("bias", C.c_void_p), ("bias_strides", C.c_int64 * 4),
     ]
 
 
@@ -124,7 +126,7 @@ def _strides4(t):
 
 
 def fill_params(q, k, v, o, lse, *, causal, scale, block_mask, mask_block, alibi, alibi_slopes_host, softcap,
-                workspace, visits) -> tuple[FwdParams, object]:
+                workspace, visits, bias=None) -> tuple[FwdParams, object]:
     """Populate odf_fwd_params from torch CUDA tensors; returns (params, keep-alive objects)."""
     import torch
 
@@ -155,6 +157,16 @@ def fill_params(q, k, v, o, lse, *, causal, scale, block_mask, mask_block, alibi
             keep.append(arr)
             p.alibi_slopes = C.cast(arr, C.c_void_p)
     p.softcap = softcap
+    if bias is not None:
+        if alibi:
+            raise ValueError("ALiBi and a bias tensor are exclusive (one BiasKind per call)")
+        # float32 CUDA tensor broadcastable to [B, Hq, M, N]; expand() gives 0 strides
+        bias_v = bias.expand(B, Hq, M, N)
+        p.bias_kind = ODF_BIAS_SAME_SHAPE
+        p.bias = bias_v.data_ptr()
+        for i, st in enumerate(bias_v.stride()):
+            p.bias_strides[i] = st
+        keep.append(bias_v)
     if workspace is not None:
         p.workspace = workspace.data_ptr()
         p.workspace_bytes = workspace.numel() * workspace.element_size()
@@ -165,8 +177,11 @@ def fill_params(q, k, v, o, lse, *, causal, scale, block_mask, mask_block, alibi
 
 def flash_fwd(q, k, v, *, causal=False, scale=None, block_mask=None, mask_block=(128, 128), alibi=False,
               alibi_slopes=None, softcap=0.0, out_dtype=None, want_lse=True, out=None, lse_out=None,
-              visits=None, stream=None):
+              visits=None, stream=None, bias=None):
     """Forward pass on CUDA tensors q [B,Hq,M,D], k [B,Hkv,N,D], v [B,Hkv,N,Dv] (bf16).
+
+    ``bias``: optional float32 CUDA tensor broadcastable to [B,Hq,M,N], added after the
+    scale (BiasKind::SameShapeTile).
 
     Returns (o [B,Hq,M,Dv], lse [B,Hq,M] fp32 natural log, or None).  The launch
     is asynchronous on ``stream`` (default: torch's current stream).
@@ -190,7 +205,7 @@ def flash_fwd(q, k, v, *, causal=False, scale=None, block_mask=None, mask_block=
         mask_t = torch.as_tensor(block_mask, dtype=torch.uint8).to(dev).contiguous()
     p, keep = fill_params(q, k, v, out, lse, causal=causal, scale=scale, block_mask=mask_t, mask_block=mask_block,
                           alibi=alibi, alibi_slopes_host=alibi_slopes, softcap=softcap, workspace=None,
-                          visits=visits)
+                          visits=visits, bias=bias)
     ws_bytes = lib.odf_fwd_workspace_size(C.byref(p))
     ws = None
     if ws_bytes:
@@ -210,7 +225,7 @@ def flash_fwd(q, k, v, *, causal=False, scale=None, block_mask=None, mask_block=
 
 
 def flash_fwd_host(q, k, v, *, causal=False, scale=None, block_mask=None, mask_block=(128, 128), alibi=False,
-                   alibi_slopes=None, softcap=0.0, out=None, lse_out=None):
+                   alibi_slopes=None, softcap=0.0, out=None, lse_out=None, bias=None):
     """Forward pass on HOST numpy buffers through odf_flash_fwd_host (blocking).
 
     q/k/v are float32 or bfloat16-as-uint16 arrays [B,H,T,D]; ``out`` (float32 or
@@ -245,7 +260,15 @@ def flash_fwd_host(q, k, v, *, causal=False, scale=None, block_mask=None, mask_b
             keep = (C.c_float * len(alibi_slopes))(*[float(x) for x in alibi_slopes])
             p.alibi_slopes = C.cast(keep, C.c_void_p)
     p.softcap = softcap
+    bias_v = None
+    if bias is not None:  # float32 array broadcastable to [B, Hq, M, N]
+        bias_v = np.broadcast_to(np.asarray(bias, dtype=np.float32), (B, Hq, M, N))
+        p.bias_kind = ODF_BIAS_SAME_SHAPE
+        p.bias = bias_v.ctypes.data
+        for i, st in enumerate(bias_v.strides):
+            p.bias_strides[i] = st // 4
     _check(lib.odf_flash_fwd_host(C.byref(p)))
+    del bias_v
     return out, lse_out
 
 

@@ -45,6 +45,7 @@ extern "C" {
 
 /* Bias kinds; values equal onednn_flash::BiasKind (score_mod_plan.hpp:21-28). */
 #define ODF_BIAS_NONE 0
+#define ODF_BIAS_SAME_SHAPE 1      /* BiasKind::SameShapeTile: fp32 tensor, see odf_fwd_params::bias */
 #define ODF_BIAS_ALIBI 4           /* BiasKind::AlibiGenerated: bias = slope[h] * (kj - qi) */
 
 #define ODF_MAX_EXPLICIT_SLOPES 256
@@ -69,7 +70,7 @@ typedef struct odf_fwd_params {
        on the device, non-zero = allowed; NULL = no block mask.  Needs a workspace. */
     const uint8_t* block_mask;
     int64_t mask_qbs, mask_kbs, mask_qblocks, mask_kblocks;
-    int32_t bias_kind;          /* ODF_BIAS_NONE or ODF_BIAS_ALIBI */
+    int32_t bias_kind;          /* ODF_BIAS_NONE, ODF_BIAS_SAME_SHAPE or ODF_BIAS_ALIBI */
     /* ALiBi slopes, HOST array [heads_q] (copied into the launch); NULL with
        ODF_BIAS_ALIBI = generated slopes 2^(-8 (h+1) / heads_q). */
     const float* alibi_slopes;
@@ -79,6 +80,15 @@ typedef struct odf_fwd_params {
     /* Optional diagnostics (device, may be NULL): u8 [B*heads_q, q_tiles, kv_tiles],
        set to 1 for every 128x128 tile the kernel processes (never cleared by it). */
     uint8_t* tile_visits;
+    /* ODF_BIAS_SAME_SHAPE (BiasKind::SameShapeTile, qk_score_tile.cpp:28-47 and 227-232):
+       s = q.k * scale + bias[b*s0 + h*s1 + qi*s2 + kj*s3] (then the soft-cap), fp32, with
+       the element strides bias_strides = {s0, s1, s2, s3} >= 0 over {batch, q-head, query,
+       key}; all zero = contiguous [B, heads_q, M, N]; otherwise zero strides broadcast
+       ({0,0,N,1}: one [M,N] matrix for every head; {0,0,0,1}: one bias per key).  Device pointer for odf_flash_fwd_sm100 (key-contiguous rows with
+       16-byte aligned starts take the vector path), host pointer for odf_flash_fwd_host.
+       Every element with qi < M and kj < N must be addressable; columns beyond N are not read. */
+    const float* bias;
+    int64_t bias_strides[4];
 } odf_fwd_params;
 
 /*

@@ -66,9 +66,16 @@ struct AttentionOptions {
     ScoreBiasFn score_bias = nullptr;    // host functor: rejected by the GPU path
 
     // ---- additions for the GPU path ----
-    // Structured bias evaluated in the kernel's epilogue: BiasKind::None or
-    // BiasKind::AlibiGenerated (bias = slope[h] * (kj - qi)).
+    // Structured bias evaluated in the kernel's epilogue: BiasKind::None,
+    // BiasKind::SameShapeTile (the `bias` tensor below) or BiasKind::AlibiGenerated
+    // (bias = slope[h] * (kj - qi)).
     BiasKind bias_kind = BiasKind::None;
+    // BiasKind::SameShapeTile: fp32 tensor in the same memory kind as q/k/v; element
+    // (b, h, qi, kj) at bias[b*s0 + h*s1 + qi*s2 + kj*s3] with bias_strides = {s0..s3};
+    // all zero = contiguous [B, H, M, N] (one [M, N] matrix for the single-head calls);
+    // otherwise zero strides broadcast.
+    const float* bias = nullptr;
+    std::int64_t bias_strides[4] = {0, 0, 0, 0};
     // Host array of per-head ALiBi slopes; nullptr = 2^(-8 (h+1) / heads).
     const float* alibi_slopes = nullptr;
     // > 0: s <- softcap * tanh(s / softcap) after scale and bias.

@@ -40,11 +40,15 @@ static inline int masked_out(const odf_oracle_params* p, int64_t qi, int64_t kj)
 }
 
 /* score * scale + score_bias(qi, kj) (attention.cpp:619), then the soft-cap. */
-static inline float score_mod(const odf_oracle_params* p, int64_t head, float score,
+static inline float score_mod(const odf_oracle_params* p, int64_t batch, int64_t head, float score,
                               int64_t qi, int64_t kj) {
     float bias = 0.0f;
     if (p->alibi_slopes != NULL) {
         bias = p->alibi_slopes[head] * (float)(kj - qi);
+    }
+    if (p->bias != NULL) {
+        bias += p->bias[batch * p->bias_strides[0] + head * p->bias_strides[1] + qi * p->bias_strides[2] +
+                        kj * p->bias_strides[3]];
     }
     float s = score * p->scale + bias;
     if (p->softcap > 0.0f) {
@@ -147,7 +151,7 @@ static void flash_head(const odf_oracle_params* p, int64_t b, int64_t h, workspa
                     const int64_t kj = k_begin + kk;
                     float* score = &ws->score[lk * k_cols + kk];
                     if (masked_out(p, qi, kj)) { *score = neg_inf; continue; }
-                    *score = score_mod(p, h, *score, qi, kj);
+                    *score = score_mod(p, b, h, *score, qi, kj);
                     block_max = ref_max(block_max, *score);
                     ws->row_has_valid[lk] = 1;
                 }
@@ -213,7 +217,7 @@ static void standard_head(const odf_oracle_params* p, int64_t b, int64_t h, floa
             if (masked_out(p, qi, kj)) { scores[kj] = -INFINITY; continue; }
             float dot = 0.0f;
             for (int64_t d = 0; d < D; ++d) dot += q[qi * D + d] * k[kj * D + d];
-            scores[kj] = score_mod(p, h, dot, qi, kj);
+            scores[kj] = score_mod(p, b, h, dot, qi, kj);
             row_max = ref_max(row_max, scores[kj]);
             has_valid = 1;
         }

@@ -16,8 +16,9 @@
  *   - soft-cap: s <- cap * tanh(s / cap), right after the scale + bias step
  *     (attention.cpp:619);
  *   - GQA: kv_head = q_head / (heads_q / heads_kv);
- *   - ALiBi as a structured additive bias slope[h] * (kj - qi), which the
- *     reference can only express through its ScoreBiasFn (attention.hpp:31).
+ *   - ALiBi as a structured additive bias slope[h] * (kj - qi), and a strided
+ *     additive bias tensor, which the reference can only express through its
+ *     ScoreBiasFn (attention.hpp:31).
  * The same struct is used by the shim over the real reference sources
  * (oracle/ref_shim.cpp), so the two can be compared call for call.
  */
@@ -48,6 +49,11 @@ typedef struct odf_oracle_params {
     const float* alibi_slopes;  /* [Hq] or NULL: bias = slope[h] * (kj - qi) */
     float softcap;              /* 0 = off */
     int nthreads;               /* threads over (batch, head); <=0 = 1 */
+    /* Additive bias tensor (BiasKind::SameShapeTile, qk_score_tile.cpp:28-47), element
+       (b, h, qi, kj) at bias[b*s0 + h*s1 + qi*s2 + kj*s3] with bias_strides = {s0..s3};
+       zero strides broadcast.  NULL = none.  Added after the scale, like score_bias. */
+    const float* bias;
+    int64_t bias_strides[4];
 } odf_oracle_params;
 
 /* Status codes shared by the oracle and the reference shim. */

@@ -36,6 +36,7 @@ class OracleParams(C.Structure):
         ("mask", C.c_void_p), ("mask_qbs", C.c_int64), ("mask_kbs", C.c_int64),
         ("mask_qblocks", C.c_int64), ("mask_kblocks", C.c_int64),
         ("alibi_slopes", C.c_void_p), ("softcap", C.c_float), ("nthreads", C.c_int),
+        ("bias", C.c_void_p), ("bias_strides", C.c_int64 * 4),
     ]
 
 
@@ -89,7 +90,7 @@ def round_bf16(x: np.ndarray) -> np.ndarray:
 
 
 def _params(q, k, v, o, lse, *, scale, causal, q_block, k_block, mask, mask_block, alibi_slopes,
-            softcap, nthreads):
+            softcap, nthreads, bias=None):
     B, Hq, M, D = q.shape
     _, Hkv, N, _ = k.shape
     DV = v.shape[3]
@@ -107,6 +108,11 @@ def _params(q, k, v, o, lse, *, scale, causal, q_block, k_block, mask, mask_bloc
     p.alibi_slopes = alibi_slopes.ctypes.data if alibi_slopes is not None else None
     p.softcap = softcap
     p.nthreads = nthreads
+    if bias is not None:  # float32 ndarray broadcastable to [B, Hq, M, N] (numpy strides, 0 = broadcast)
+        bias = np.broadcast_to(bias, (B, Hq, M, N))
+        p.bias = bias.ctypes.data
+        for i in range(4):
+            p.bias_strides[i] = bias.strides[i] // 4
     return p
 
 
@@ -124,8 +130,10 @@ def _prep(q, k, v, mask, alibi_slopes):
 
 
 def _run(fn_name, lib, q, k, v, *, scale=None, causal=False, q_block=128, k_block=128, mask=None,
-         mask_block=(128, 128), alibi_slopes=None, softcap=0.0, want_lse=True, nthreads=None):
+         mask_block=(128, 128), alibi_slopes=None, softcap=0.0, want_lse=True, nthreads=None, bias=None):
     q, k, v, mask, alibi_slopes = _prep(q, k, v, mask, alibi_slopes)
+    if bias is not None:
+        bias = np.asarray(bias, dtype=np.float32)
     B, Hq, M, D = q.shape
     if scale is None:
         scale = 1.0 / float(np.sqrt(D))
@@ -134,7 +142,7 @@ def _run(fn_name, lib, q, k, v, *, scale=None, causal=False, q_block=128, k_bloc
     if nthreads is None:
         nthreads = max(1, min(os.cpu_count() or 1, 64))
     p = _params(q, k, v, o, lse, scale=scale, causal=causal, q_block=q_block, k_block=k_block, mask=mask,
-                mask_block=mask_block, alibi_slopes=alibi_slopes, softcap=softcap, nthreads=nthreads)
+                mask_block=mask_block, alibi_slopes=alibi_slopes, softcap=softcap, nthreads=nthreads, bias=bias)
     rc = getattr(lib, fn_name)(C.byref(p))
     if rc != 0:
         raise RuntimeError(f"{fn_name} failed with status {rc}")

@@ -51,11 +51,19 @@ bool make_options(const odf_oracle_params* p, of::BlockMask* mask_storage, of::A
     return p->softcap == 0.0f;  // soft-cap does not exist in the reference
 }
 
-of::ScoreBiasFn alibi_fn(const odf_oracle_params* p, int64_t h) {
-    if (!p->alibi_slopes) return nullptr;
-    const float slope = p->alibi_slopes[h];
-    return [slope](std::size_t qi, std::size_t kj) {
-        return slope * static_cast<float>(static_cast<int64_t>(kj) - static_cast<int64_t>(qi));
+// The structured biases of odf_oracle_params as the reference's ScoreBiasFn (attention.hpp:31)
+// for one (batch, q-head): ALiBi slope[h] * (kj - qi), a strided bias tensor, or their sum.
+of::ScoreBiasFn bias_fn(const odf_oracle_params* p, int64_t b, int64_t h) {
+    if (!p->alibi_slopes && !p->bias) return nullptr;
+    const float slope = p->alibi_slopes ? p->alibi_slopes[h] : 0.0f;
+    const bool has_alibi = p->alibi_slopes != nullptr;
+    const float* bias = p->bias ? p->bias + b * p->bias_strides[0] + h * p->bias_strides[1] : nullptr;
+    const int64_t sm = p->bias_strides[2], sn = p->bias_strides[3];
+    return [=](std::size_t qi, std::size_t kj) {
+        float v = 0.0f;
+        if (has_alibi) v = slope * static_cast<float>(static_cast<int64_t>(kj) - static_cast<int64_t>(qi));
+        if (bias) v += bias[static_cast<int64_t>(qi) * sm + static_cast<int64_t>(kj) * sn];
+        return v;
     };
 }
 
@@ -88,7 +96,7 @@ int run(const odf_oracle_params* p, Variant variant) {
                 const float* v = p->v + (b * p->heads_kv + hk) * p->n * p->dv;
                 float* o = p->o + (b * p->heads_q + h) * p->m * p->dv;
                 of::AttentionOptions opt = base;
-                opt.score_bias = alibi_fn(p, h);
+                opt.score_bias = bias_fn(p, b, h);
                 if (variant == Variant::Ws) {
                     std::fill(o, o + p->m * p->dv, 0.0f);  // rows with l <= 0 stay as the caller left them
                     of::flash_attention_qk_pv_tile_ws(q, k, v, o, shape, opt, ws);
@@ -140,7 +148,7 @@ int odf_ref_qk_pv_tile(const odf_oracle_params* p) { return run(p, Variant::QkPv
 // flash_attention_batched_qk_pv_tile as shipped: serial, one thread_local workspace,
 // heads of Q/K/V equal (no GQA), no bias functor.
 int odf_ref_batched(const odf_oracle_params* p) {
-    if (!p || p->heads_q != p->heads_kv || p->alibi_slopes || p->lse) return ODF_ORACLE_EUNSUPPORTED;
+    if (!p || p->heads_q != p->heads_kv || p->alibi_slopes || p->bias || p->lse) return ODF_ORACLE_EUNSUPPORTED;
     of::BlockMask mask;
     of::AttentionOptions opt;
     if (!make_options(p, &mask, &opt)) return ODF_ORACLE_EUNSUPPORTED;

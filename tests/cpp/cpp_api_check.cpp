@@ -122,9 +122,10 @@ void planner() {
 }
 
 // Case file (little endian): int32 header[16], float params[4], then q, k, v (fp32), then
-// an optional u8 mask, then optional fp32 alibi slopes.
+// an optional u8 mask, then optional fp32 alibi slopes [H] (bias = 1) or an fp32 bias
+// tensor [B, H, M, N] (bias = 2, BiasKind::SameShapeTile with contiguous strides).
 //   header: api, B, H, Hkv, M, N, D, DV, causal, q_block, k_block, mask_qbs, mask_kbs,
-//           mask_qblocks, mask_kblocks, bias_alibi
+//           mask_qblocks, mask_kblocks, bias
 //   params: scale, softcap, want_lse, device_pointers
 //   api: 0 standard_attention, 1 flash_attention_tiled, 2 flash_attention_q_tile,
 //        3 flash_attention_qk_pv_tile, 4 flash_attention_qk_pv_tile_ws,
@@ -152,10 +153,13 @@ int run_case(const char* in_path, const char* out_path) {
         mask.allowed.resize(static_cast<size_t>(hd[13]) * hd[14]);
         if (std::fread(mask.allowed.data(), 1, mask.allowed.size(), f) != mask.allowed.size()) return 3;
     }
-    std::vector<float> slopes;
-    if (hd[15]) {
+    std::vector<float> slopes, bias;
+    if (hd[15] == 1) {
         slopes.resize(H);
         if (std::fread(slopes.data(), 4, H, f) != static_cast<size_t>(H)) return 3;
+    } else if (hd[15] == 2) {
+        bias.resize(static_cast<size_t>(B) * H * M * N);
+        if (std::fread(bias.data(), 4, bias.size(), f) != bias.size()) return 3;
     }
     std::fclose(f);
 
@@ -166,9 +170,12 @@ int run_case(const char* in_path, const char* out_path) {
     opt.key_block_size = static_cast<size_t>(hd[10]);
     opt.block_mask = has_mask ? &mask : nullptr;
     opt.softcap = pr[1];
-    if (hd[15]) {
+    if (hd[15] == 1) {
         opt.bias_kind = of::BiasKind::AlibiGenerated;
         opt.alibi_slopes = slopes.data();
+    } else if (hd[15] == 2) {
+        opt.bias_kind = of::BiasKind::SameShapeTile;
+        opt.bias = bias.data();  // all-zero strides: contiguous [B, H, M, N]
     }
     opt.kv_heads = static_cast<size_t>(Hkv);
     std::vector<float> lse(static_cast<size_t>(B) * H * M, 0.0f);
@@ -194,7 +201,7 @@ int run_case(const char* in_path, const char* out_path) {
             const bool on_device = pr[3] != 0.0f;
             const float *pq = q.data(), *pk = k.data(), *pv = v.data();
             float* po = out.data();
-            float *dq = nullptr, *dk = nullptr, *dv = nullptr, *dout = nullptr, *dlse = nullptr;
+            float *dq = nullptr, *dk = nullptr, *dv = nullptr, *dout = nullptr, *dlse = nullptr, *dbias = nullptr;
             if (on_device) {
                 if (cudaMalloc(&dq, q.size() * 4) || cudaMalloc(&dk, k.size() * 4) || cudaMalloc(&dv, v.size() * 4) ||
                     cudaMalloc(&dout, out.size() * 4) || cudaMalloc(&dlse, lse.size() * 4))
@@ -204,6 +211,11 @@ int run_case(const char* in_path, const char* out_path) {
                 cudaMemcpy(dv, v.data(), v.size() * 4, cudaMemcpyHostToDevice);
                 pq = dq; pk = dk; pv = dv; po = dout;
                 if (opt.lse) opt.lse = dlse;
+                if (!bias.empty()) {
+                    if (cudaMalloc(&dbias, bias.size() * 4)) throw std::runtime_error("test driver: cudaMalloc failed");
+                    cudaMemcpy(dbias, bias.data(), bias.size() * 4, cudaMemcpyHostToDevice);
+                    opt.bias = dbias;
+                }
             }
             if (api == 4) {
                 of::AttentionWorkspace ws;
@@ -219,6 +231,7 @@ int run_case(const char* in_path, const char* out_path) {
                 cudaMemcpy(out.data(), dout, out.size() * 4, cudaMemcpyDeviceToHost);
                 cudaMemcpy(lse.data(), dlse, lse.size() * 4, cudaMemcpyDeviceToHost);
                 cudaFree(dq); cudaFree(dk); cudaFree(dv); cudaFree(dout); cudaFree(dlse);
+                if (dbias) cudaFree(dbias);
             }
         }
     } catch (const std::invalid_argument& e) {

@@ -50,7 +50,8 @@ def _params(**over):
     ("o_dtype", 7, odf_b200.ODF_ERR_UNSUPPORTED),
     ("softcap", -1.0, odf_b200.ODF_ERR_INVALID_ARG),
     ("scale", float("inf"), odf_b200.ODF_ERR_INVALID_ARG),
-    ("bias_kind", 1, odf_b200.ODF_ERR_UNSUPPORTED),  # BiasKind::SameShapeTile: not on the GPU yet
+    ("bias_kind", odf_b200.ODF_BIAS_SAME_SHAPE, odf_b200.ODF_ERR_INVALID_ARG),  # SameShapeTile without a tensor
+    ("bias_kind", 2, odf_b200.ODF_ERR_UNSUPPORTED),  # BiasKind::BroadcastRow: a strided SameShapeTile here
     ("seqlen_q", 65536 * 128, odf_b200.ODF_ERR_UNSUPPORTED),
 ])
 def test_validation_codes(field, value, code):
@@ -58,6 +59,17 @@ def test_validation_codes(field, value, code):
     rc = lib.odf_flash_fwd_sm100(C.byref(_params(**{field: value})), None)
     assert rc == code
     assert odf_b200.last_error()
+
+
+def test_same_shape_bias_checks():
+    lib = odf_b200.load_library()
+    p = _params(bias_kind=odf_b200.ODF_BIAS_SAME_SHAPE, bias=4096)
+    p.bias_strides[2] = -1
+    assert lib.odf_flash_fwd_sm100(C.byref(p), None) == odf_b200.ODF_ERR_INVALID_ARG
+    assert "stride" in odf_b200.last_error()
+    p = _params(bias_kind=odf_b200.ODF_BIAS_SAME_SHAPE, bias=4098)
+    assert lib.odf_flash_fwd_sm100(C.byref(p), None) == odf_b200.ODF_ERR_INVALID_ARG
+    assert "aligned" in odf_b200.last_error()
 
 
 def test_block_mask_needs_sizes_and_workspace():

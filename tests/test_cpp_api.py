@@ -90,14 +90,14 @@ APIS = {"standard": 0, "tiled": 1, "q_tile": 2, "qk_pv_tile": 3, "ws": 4, "batch
 
 
 def run_api(driver, tmp_path, api, q, k, v, *, causal=False, scale=None, q_block=16, k_block=32, mask=None,
-            mask_block=(1, 1), slopes=None, softcap=0.0, want_lse=True, device=False):
+            mask_block=(1, 1), slopes=None, softcap=0.0, want_lse=True, device=False, bias=None):
     B, H, M, D = q.shape
     _, Hkv, N, _ = k.shape
     DV = v.shape[3]
     scale = 1.0 / np.sqrt(D) if scale is None else scale
     hdr = [APIS[api], B, H, Hkv, M, N, D, DV, int(causal), q_block, k_block, mask_block[0], mask_block[1],
            mask.shape[0] if mask is not None else 0, mask.shape[1] if mask is not None else 0,
-           int(slopes is not None)]
+           1 if slopes is not None else (2 if bias is not None else 0)]
     inp = tmp_path / f"{api}_in.bin"
     outp = tmp_path / f"{api}_out.bin"
     with open(inp, "wb") as f:
@@ -109,6 +109,8 @@ def run_api(driver, tmp_path, api, q, k, v, *, causal=False, scale=None, q_block
             f.write(np.ascontiguousarray(mask, dtype=np.uint8).tobytes())
         if slopes is not None:
             f.write(np.asarray(slopes, dtype=np.float32).tobytes())
+        elif bias is not None:
+            f.write(np.ascontiguousarray(np.broadcast_to(bias, (B, H, M, N)), dtype=np.float32).tobytes())
     proc = subprocess.run([str(driver), "run", str(inp), str(outp)], capture_output=True, text=True)
     assert proc.returncode == 0, proc.stderr
     raw = np.fromfile(outp, dtype=np.uint8)
@@ -163,6 +165,21 @@ def test_batched_entry_point_gqa_softcap(driver, tmp_path, device):
     assert status == 0, err
     o_ref, lse_ref = oracle.flash_fwd(q, k, v, causal=True, softcap=30.0)
     close(o, lse, o_ref, lse_ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("device", [False, True])
+@pytest.mark.parametrize("api", ["ws", "batched"])
+def test_same_shape_bias_through_cpp_api(driver, tmp_path, device, api):
+    """AttentionOptions{bias_kind = SameShapeTile, bias} on host and device pointers, against the
+    oracle (equal to the reference's ScoreBiasFn path bit for bit, test_oracle_vs_reference.py)."""
+    B, H = (1, 1) if api == "ws" else (2, 4)
+    q, k, v = make_qkv(66, B, H, H, 270, 300, 128)
+    bias = (np.random.default_rng(67).standard_normal((B, H, 270, 300)) * 2.0).astype(np.float32)
+    status, o, lse, err = run_api(driver, tmp_path, api, q, k, v, causal=True, bias=bias, device=device)
+    assert status == 0, err
+    r, lse_ref = oracle.flash_fwd(q, k, v, causal=True, q_block=16, k_block=32, bias=bias)
+    close(o, lse, r, lse_ref)
 
 
 @pytest.mark.gpu

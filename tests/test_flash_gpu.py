@@ -329,6 +329,75 @@ def test_config5_full_size_prefix_and_tail():
         assert np.abs(lse[0, h, rows].cpu().numpy() - lse64).max() <= LSE_MAX_ABS
 
 
+# --------------------------------------------------------------------------- same-shape bias
+def _bias(seed, shape, scale=2.0):
+    rng = np.random.default_rng(seed)
+    return (rng.standard_normal(shape) * scale).astype(np.float32)
+
+
+@pytest.mark.parametrize("case", ["full_gqa_causal", "head_broadcast", "key_row_softcap", "strided_keys",
+                                  "query_col", "mask", "d64_softcap"])
+def test_same_shape_bias(case):
+    """BiasKind::SameShapeTile (qk_score_tile.cpp:28-47): s*scale + bias[b,h,qi,kj] (then soft-cap),
+    with broadcast and strided bias layouts, against the oracle (itself pinned to the reference's
+    ScoreBiasFn path)."""
+    torch = _torch()
+    import oracle
+
+    B, H, Hk, M, N, D = 2, 4, 2, 300, 300, 128
+    kw, okw = {}, {}
+    if case == "full_gqa_causal":
+        bias = _bias(1, (B, H, M, N))
+        kw["causal"] = okw["causal"] = True
+    elif case == "head_broadcast":
+        bias = _bias(2, (1, 1, M, N))
+    elif case == "key_row_softcap":
+        bias = _bias(3, (1, 1, 1, N))
+        kw["causal"] = okw["causal"] = True
+        kw["softcap"] = okw["softcap"] = 30.0
+    elif case == "strided_keys":  # bias[..., ::2] of a wider tensor: key stride 2 (scalar path)
+        wide = _bias(4, (B, H, M, 2 * N))
+        bias = wide[..., ::2]
+    elif case == "query_col":
+        bias = _bias(5, (B, 1, M, 1))
+        kw["causal"] = okw["causal"] = True
+    elif case == "mask":
+        bias = _bias(6, (1, H, M, N))
+        mask = oracle.sliding_window_prefix_mask(3, 1, 1)
+        kw.update(causal=True, block_mask=mask, mask_block=(128, 128))
+        okw.update(causal=True, mask=mask, mask_block=(128, 128))
+    else:  # d64_softcap
+        D = 64
+        bias = _bias(7, (B, H, M, N))
+        kw["softcap"] = okw["softcap"] = 20.0
+    q, k, v = make_qkv(30, B, H, Hk, M, N, D)
+    if case == "strided_keys":
+        dev_bias = to_dev(wide, torch.float32)[..., ::2]
+        assert dev_bias.stride(3) == 2
+    else:
+        dev_bias = to_dev(bias, torch.float32)
+    o, lse = run_gpu(q, k, v, bias=dev_bias, **kw)
+    o_ref, lse_ref = oracle_fwd(q, k, v, bias=bias, **okw)
+    check_close(o, lse, o_ref, lse_ref, f"bias {case}")
+
+
+def test_same_shape_bias_host_entry():
+    """The host entry stages each (batch, head) bias plane (or one broadcast plane) per chunk and
+    equals the device entry on the same values."""
+    import odf_b200
+
+    B, H, Hk, M, N, D = 2, 8, 2, 257, 333, 128
+    q, k, v = make_qkv(31, B, H, Hk, M, N, D)
+    for bias in (_bias(8, (B, H, M, N)), _bias(9, (1, 1, M, N)), _bias(10, (1, 1, 1, N))):
+        lse = np.empty((B, H, M), dtype=np.float32)
+        o, _ = odf_b200.flash_fwd_host(q, k, v, causal=True, bias=bias, lse_out=lse)
+        o_dev, lse_dev = run_gpu(q, k, v, causal=True, bias=to_dev(bias, _torch().float32))
+        assert np.array_equal(o, o_dev)
+        assert np.array_equal(lse, lse_dev)
+        o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, bias=bias)
+        check_close(o, lse, o_ref, lse_ref, "bias host entry")
+
+
 # --------------------------------------------------------------------------- host entry / status
 @pytest.mark.parametrize("in_dtype", ["f32", "bf16"])
 def test_host_entry_matches_device_entry(in_dtype):

@@ -36,6 +36,31 @@ def test_alibi_blockmask_gqa_bit_exact():
 
 
 @needs_ref
+@pytest.mark.parametrize("layout", ["full", "head_broadcast", "key_row", "strided"])
+@pytest.mark.parametrize("causal", [False, True])
+def test_bias_tensor_bit_exact(layout, causal):
+    """The oracle's strided bias tensor (BiasKind::SameShapeTile on the GPU) equals the reference
+    given the same values through its ScoreBiasFn (attention.cpp:619), for the flash and the
+    materialising paths."""
+    rng = np.random.default_rng(7)
+    B, H, M, N = 2, 3, 150, 170
+    q, k, v = make_qkv(26, B, H, H, M, N, 32)
+    if layout == "full":
+        bias = rng.standard_normal((B, H, M, N)).astype(np.float32)
+    elif layout == "head_broadcast":
+        bias = rng.standard_normal((1, 1, M, N)).astype(np.float32)
+    elif layout == "key_row":
+        bias = rng.standard_normal((1, 1, 1, N)).astype(np.float32)
+    else:
+        bias = rng.standard_normal((B, H, M, 2 * N)).astype(np.float32)[..., ::2]
+    kw = dict(causal=causal, q_block=16, k_block=32, bias=bias)
+    o, _ = oracle.flash_fwd(q, k, v, **kw)
+    assert np.array_equal(o, oracle.ref_fwd("flash_ws", q, k, v, **kw))
+    s, _ = oracle.standard_fwd(q, k, v, causal=causal, bias=bias)
+    assert np.array_equal(s, oracle.ref_fwd("standard", q, k, v, causal=causal, bias=bias))
+
+
+@needs_ref
 @pytest.mark.parametrize("variant", ["standard", "tiled", "q_tile", "qk_pv_tile"])
 def test_other_reference_entry_points_agree(variant):
     """standard_attention / flash_attention_tiled / _q_tile / _qk_pv_tile (attention.cpp:88-484)."""
