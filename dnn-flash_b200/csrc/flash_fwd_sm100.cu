@@ -18,16 +18,19 @@
 //              it also owns the TMEM allocation
 //   warp  9    MMA issuer (one thread)
 //   warps 10-11 idle
-// setmaxnreg moves registers from warpgroup 2 (168 -> 88) to the softmax warpgroups
-// (168 -> 208), which hold a whole 128-column S row per thread.  The roles never meet in
+// setmaxnreg moves registers from warpgroup 2 (168 -> 104) to the softmax warpgroups
+// (168 -> 200), which hold a whole 128-column S row per thread.  The roles never meet in
 // common code after the split (each ends with its own CTA barrier), so ptxas allocates
 // each under its own budget.
 // Tensor memory (512 columns):
 //   S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D,256+2D)
-//   P_i (bf16, two per column) is written over the first 64 columns of S_i and is
-//   the A operand of the P.V MMA read straight from tensor memory.
+//   P_i (bf16, two per column) is the A operand of the P.V MMA read straight from tensor
+//   memory.  D = 128: P_i is written over the first 64 columns of S_i.  D = 64: P_i has its
+//   own columns [384 + 64 i, 448 + 64 i), so S_i(j+1) is issued once the softmax has read
+//   S_i(j) (barrier s_free) and the softmax waits for P.V(j-1) (barrier pv_done) before it
+//   overwrites P_i or rescales O_i.
 // MMA issue order per KV tile j (in-order execution on the tensor core):
-//   PV0(j), S0(j+1), PV1(j), S1(j+1)
+//   D = 128: PV0(j), S0(j+1), PV1(j), S1(j+1);  D = 64: S0(j+1), S1(j+1), PV0(j), PV1(j)
 // and at an item's last tile PV0, PV1 (committed to o_done[0/1]) then S0, S1 of the next item
 // so while the softmax of one query tile runs, the tensor core works on the other
 // tile's P.V and S MMAs.  S_i(j+1) overwrites S_i/P_i only after PV_i(j) was issued.
@@ -60,8 +63,8 @@ constexpr int kWarpMma = 9;    // warps 10 and 11 only give their registers away
 // kRegsSoftmax, which must not exceed what the block was launched with.  The host checks
 // the compiled register count before the first launch.
 constexpr int kLaunchRegs = 168;
-constexpr int kRegsCtrl = 88;
-constexpr int kRegsSoftmax = 208;
+constexpr int kRegsCtrl = 104;
+constexpr int kRegsSoftmax = 200;
 static_assert(128 * kRegsCtrl + 256 * kRegsSoftmax <= kThreads * kLaunchRegs, "register split exceeds the launch");
 static_assert(kRegsCtrl % 8 == 0 && kRegsSoftmax % 8 == 0 && kRegsSoftmax <= 256, "setmaxnreg operands");
 constexpr uint32_t kTmemCols = 512;
@@ -83,10 +86,15 @@ struct Config {
     static constexpr uint32_t kTileBytes = 128 * D * 2;
     static constexpr uint32_t kOffSlots = 2 * kTileBytes;
     static constexpr uint32_t kOffBar = kOffSlots + kSlots * kTileBytes;
-    static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 1;
+    static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 2 + 2 + 1;
     static constexpr uint32_t kOffRows = kOffBar + kNumBars * 8 + 16;  // after the barriers, TMEM slot, abort flag
     static constexpr uint32_t kSmemBytes = kOffRows + 8 * 40 + 1024;     // + alignment slack
     static constexpr uint32_t kTmemO = 256;
+    // D = 64 leaves 128 TMEM columns free: P_i gets its own 64 columns at kTmemP + 64 i, so that
+    // S_i(j+1) can be computed as soon as the softmax has loaded S_i(j) (instead of after
+    // P.V(j) has read P_i(j) out of S_i's columns).
+    static constexpr bool kSepP = (D == 64);
+    static constexpr uint32_t kTmemP = 384;
 };
 
 struct Bars {
@@ -97,6 +105,8 @@ struct Bars {
     uint64_t* s_full;   // [2]
     uint64_t* p_full;   // [2]
     uint64_t* o_done;   // [2]
+    uint64_t* s_free;   // [2] separate-P layout: the softmax has read S_i into registers
+    uint64_t* pv_done;  // [2] separate-P layout: P_i.V has completed (P_i may be overwritten)
     uint64_t* drain;
 };
 
@@ -274,7 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars.s_full = bars.slot_empty + kSlots;
     bars.p_full = bars.s_full + 2;
     bars.o_done = bars.p_full + 2;
-    bars.drain = bars.o_done + 2;
+    bars.s_free = bars.o_done + 2;
+    bars.pv_done = bars.s_free + 2;
+    bars.drain = bars.pv_done + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars.drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -293,6 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&bars.s_full[i], 1);
             ptx::mbar_init(&bars.p_full[i], 128);
             ptx::mbar_init(&bars.o_done[i], 1);
+            ptx::mbar_init(&bars.s_free[i], 128);
+            ptx::mbar_init(&bars.pv_done[i], 1);
         }
         ptx::mbar_init(bars.drain, 1);
         *abort_flag = 0;
@@ -384,12 +398,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t v_lo0 = ptx::sdesc_sw128_lo(ptx::smem_u32(sSlots), kChunkBytes);
                 constexpr uint32_t kSlotStep = Cfg::kTileBytes >> 4;  // descriptor units per ring slot
                 int pv_count[2] = {0, 0};     // P.V MMAs so far (parity of p_full)
+                int s_count[2] = {0, 0};      // S MMAs so far (separate-P layout: parity of s_free)
                 bool acc[2] = {false, false};  // O_i already holds a P.V of the current item
                 int q_loads = 0;
                 bool ok = true;
 
                 // S_i = Q_i K^T (SS, M=128, N=128, K=D) into TMEM columns [128 i, 128 i + 128).
-                auto issue_s = [&](int i, int slot) {
+                // Separate-P layout: S_i is overwritten once the softmax has read the previous one.
+                auto issue_s = [&](int i, int slot) -> bool {
+                    if (Cfg::kSepP && s_count[i] > 0) {
+                        if (!ptx::mbar_wait(&bars.s_free[i], (s_count[i] - 1) & 1, abort_flag, args.status,
+                                            ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
+                            return false;
+                        ptx::tc_fence_after();
+                    }
+                    ++s_count[i];
                     const uint32_t qd = i == 0 ? q_lo0 : q_lo1;
                     const uint32_t kd = k_lo0 + static_cast<uint32_t>(slot) * kSlotStep;
 #pragma unroll
@@ -398,6 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ptx::mma_bf16_ss_lo(tmem + i * 128, qd + off, kd + off, kDescHi, kIdescQK, kk > 0 ? 1u : 0u);
                     }
                     ptx::tc_commit(&bars.s_full[i]);
+                    return true;
                 };
                 // O_i += P_i V (TS: P_i from TMEM, V MN-major from shared memory; M=128, N=D, K=128).
                 auto issue_pv = [&](int i, int slot) -> bool {
@@ -409,10 +433,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t first = acc[i] ? 1u : 0u;
 #pragma unroll
                     for (int kk = 0; kk < kTileK / 16; ++kk) {
-                        ptx::mma_bf16_ts_lo(tmem + Cfg::kTmemO + i * D, tmem + i * 128 + kk * 8,
+                        ptx::mma_bf16_ts_lo(tmem + Cfg::kTmemO + i * D,
+                                            tmem + (Cfg::kSepP ? Cfg::kTmemP + i * 64 : i * 128) + kk * 8,
                                             vd + static_cast<uint32_t>(kk * (2048 >> 4)), kDescHi, kIdescPV,
                                             (first | kk) ? 1u : 0u);
                     }
+                    if (Cfg::kSepP) ptx::tc_commit(&bars.pv_done[i]);
                     acc[i] = true;
                     ++pv_count[i];
                     return true;
@@ -429,8 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ++q_loads;
                     if (!wait_full(tk)) return false;
                     ptx::tc_fence_after();
-                    if (en & kNeed0) issue_s(0, tk % kSlots);
-                    if (en & kNeed1) issue_s(1, tk % kSlots);
+                    if ((en & kNeed0) && !issue_s(0, tk % kSlots)) return false;
+                    if ((en & kNeed1) && !issue_s(1, tk % kSlots)) return false;
                     ptx::tc_commit(&bars.slot_empty[tk % kSlots]);
                     if (In.n_entries == 1) ptx::tc_commit(bars.q_empty);
                     return true;
@@ -447,15 +473,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const bool last = j + 1 == I.n_entries;
                     if (!(ok = wait_full(tv))) break;
                     ptx::tc_fence_after();
-                    if (!last) {
+                    if (!last && Cfg::kSepP) {
+                        // separate P: the next S MMAs go first (they only wait for the softmax to
+                        // have read S), then this tile's P.V MMAs as each P_i arrives
+                        const uint32_t en = kv_entry(args, I, j + 1);
+                        if (!(ok = wait_full(tk))) break;
+                        ptx::tc_fence_after();
+                        if ((en & kNeed0) && !(ok = issue_s(0, tk % kSlots))) break;
+                        if ((en & kNeed1) && !(ok = issue_s(1, tk % kSlots))) break;
+                        ptx::tc_commit(&bars.slot_empty[tk % kSlots]);
+                        if (j + 2 == I.n_entries) ptx::tc_commit(bars.q_empty);  // last S MMAs of the item issued
+                        if ((e & kNeed0) && !(ok = issue_pv(0, tv % kSlots))) break;
+                        if ((e & kNeed1) && !(ok = issue_pv(1, tv % kSlots))) break;
+                        ptx::tc_commit(&bars.slot_empty[tv % kSlots]);
+                        e = en;
+                        ++j;
+                    } else if (!last) {
                         const uint32_t en = kv_entry(args, I, j + 1);
                         if ((e & kNeed0) && !(ok = issue_pv(0, tv % kSlots))) break;
                         if (!(ok = wait_full(tk))) break;
                         ptx::tc_fence_after();
-                        if (en & kNeed0) issue_s(0, tk % kSlots);
+                        if ((en & kNeed0) && !(ok = issue_s(0, tk % kSlots))) break;
                         if ((e & kNeed1) && !(ok = issue_pv(1, tv % kSlots))) break;
                         ptx::tc_commit(&bars.slot_empty[tv % kSlots]);
-                        if (en & kNeed1) issue_s(1, tk % kSlots);
+                        if ((en & kNeed1) && !(ok = issue_s(1, tk % kSlots))) break;
                         ptx::tc_commit(&bars.slot_empty[tk % kSlots]);
                         if (j + 2 == I.n_entries) ptx::tc_commit(bars.q_empty);  // last S MMAs of the item issued
                         e = en;
@@ -500,8 +541,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
         const uint32_t s_addr = tmem + lane_off + qtile * 128;
         const uint32_t o_addr = tmem + lane_off + Cfg::kTmemO + qtile * D;
+        const uint32_t p_addr = tmem + lane_off + (Cfg::kSepP ? Cfg::kTmemP + qtile * 64 : qtile * 128);
         // bit 0: parity of the next s_full wait, bit 1: of the next o_done wait,
-        // bit 2: the current item has fed O_i (at least one S_i tile processed)
+        // bit 2: the current item has fed O_i (at least one S_i tile processed),
+        // bit 3: parity of the next pv_done wait, bit 4: a P_i was stored before (separate-P layout)
         uint32_t phases = 0;
         bool ok = true;
 
@@ -545,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             float m_run = -INFINITY;  // running (reference) max, log2 units
             float l_run = 0.0f;       // running sum relative to m_run
-            phases &= 3u;
+            phases &= ~4u;
 
             const int n_iter = rec->n_iter;
             for (int j = 0; j < n_iter; ++j) {
@@ -574,6 +617,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 float s[128];
                 ptx::tmem_ld128(s_addr, s);
+                if (Cfg::kSepP) {  // S_i is in registers: the next S_i may be computed now
+                    ptx::tc_fence_before();
+                    ptx::mbar_arrive(&bars.s_free[qtile]);
+                }
                 if (row == 0 && args.visits) {
                     args.visits[(static_cast<int64_t>(rec->bh) * args.n_qt + (q0 / kTileQ)) * args.n_kt + kt] = 1;
                 }
@@ -700,8 +747,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint64_t sum_all = ptx::fadd2(ptx::fadd2(sum2[0], sum2[1]), ptx::fadd2(sum2[2], sum2[3]));
                 l_run = l_run * alpha + (ptx::lo_f32(sum_all) + ptx::hi_f32(sum_all));
 
+                // Separate-P layout: the previous P_i.V must have completed before P_i is overwritten
+                // and before O_i is rescaled (S_i(j) can complete ahead of it there).
+                if (Cfg::kSepP && (phases & 16u)) {
+                    const bool done = ptx::mbar_wait(&bars.pv_done[qtile], (phases >> 3) & 1u, abort_flag,
+                                                     args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+                    phases ^= 8u;
+                    if (!__all_sync(0xffffffffu, done)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                }
+                phases |= 16u;
                 // correction: O_i *= alpha when the reference max moved (PV_i of the previous
-                // tile is complete: the commit that released S_i(j) covers every earlier MMA)
+                // tile is complete: the commit that released S_i(j) covers every earlier MMA, and
+                // the separate-P layout waited for it above)
                 if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
                     for (int c = 0; c < D / 32; ++c) {
@@ -712,8 +773,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ptx::tmem_st32_nowait(o_addr + c * 32, reinterpret_cast<const uint32_t*>(o));
                     }
                 }
-                // P_i over the first 64 columns of S_i, the A operand of PV_i
-                ptx::tmem_st64_nowait(s_addr, reinterpret_cast<const uint32_t*>(s));
+                // P_i (over the first 64 columns of S_i, or its own columns for D = 64), the A
+                // operand of PV_i
+                ptx::tmem_st64_nowait(p_addr, reinterpret_cast<const uint32_t*>(s));
                 ptx::tmem_st_wait();
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&bars.p_full[qtile]);
