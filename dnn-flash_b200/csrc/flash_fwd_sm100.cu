@@ -234,6 +234,37 @@ __device__ __forceinline__ uint4 row_allow_bits(const FwdArgs& a, int qi, int k0
     return allow;
 }
 
+// 2^x for a pair on the FMA pipe.  At d = 64 the MUFU unit (16 ex2 per clock per SM) is the
+// binding limit, so part of the columns take this path instead.  x is clamped to -127, split as
+// x = j + f with j = rint(x) (by adding and subtracting 1.5 * 2^23) and f in [-0.5, 0.5]; 2^f
+// comes from a degree-3 polynomial whose coefficients were fitted here for minimax relative
+// error with p(0) = 1 (max relative error 1.0e-4), and j is added to the exponent field.
+// x = -127 (so also -inf) gives exactly +0; other x below -126 give values in [0, 2^-126).
+constexpr float kExp2C1 = 0.6932829022407532f;
+constexpr float kExp2C2 = 0.2422109693288803f;
+constexpr float kExp2C3 = 0.055009059607982635f;
+
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+    const uint64_t xc = ptx::f32x2(fmaxf(ptx::lo_f32(x), -127.0f), fmaxf(ptx::hi_f32(x), -127.0f));
+    const uint64_t t = ptx::fadd2(xc, ptx::f32x2(12582912.0f));   // 1.5 * 2^23 + rint(x)
+    const uint64_t j = ptx::fadd2(t, ptx::f32x2(-12582912.0f));   // rint(x), exact
+    const uint64_t f = ptx::ffma2(j, ptx::f32x2(-1.0f), xc);      // x - rint(x), exact
+    uint64_t p = ptx::ffma2(ptx::f32x2(kExp2C3), f, ptx::f32x2(kExp2C2));
+    p = ptx::ffma2(p, f, ptx::f32x2(kExp2C1));
+    p = ptx::ffma2(p, f, ptx::f32x2(1.0f));
+    // the low bits of t hold 1.5 * 2^23 + j; shifted left by 23 only j << 23 remains (mod 2^32)
+    const uint32_t lo = static_cast<uint32_t>(p) + (static_cast<uint32_t>(t) << 23);
+    const uint32_t hi = static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
+    return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
+// Column pairs (index c/2 mod 8) whose exponentials use exp2_poly2, per head dim.
+#ifndef ODF_POLY_MASK_D64
+#define ODF_POLY_MASK_D64 0x80  // one pair in eight: the best of 0, 1/8, 1/4, 3/8, 1/2 measured at d = 64
+#endif
+template <int D>
+__host__ __device__ constexpr uint32_t poly_exp2_mask() { return D == 64 ? ODF_POLY_MASK_D64 : 0u; }
+
 // Reciprocal of a pair d in (1, 2] on the FMA pipe: integer-subtraction seed (constant
 // fitted here for <= 5.1% relative error) and three Newton steps r <- r (2 - d r) (~1.5e-7).
 __device__ __forceinline__ uint64_t rcp2_1to2(uint64_t d) {
@@ -738,8 +769,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int c = 0; c < 128; c += 2) {
                         const uint64_t x = ptx::ffma2(ptx::f32x2(s[c], s[c + 1]), mul2, neg2);
-                        const float p0 = ptx::ex2(ptx::lo_f32(x));
-                        const float p1 = ptx::ex2(ptx::hi_f32(x));
+                        float p0, p1;
+                        if ((poly_exp2_mask<D>() >> ((c >> 1) & 7)) & 1u) {
+                            const uint64_t p = exp2_poly2(x);
+                            p0 = ptx::lo_f32(p);
+                            p1 = ptx::hi_f32(p);
+                        } else {
+                            p0 = ptx::ex2(ptx::lo_f32(x));
+                            p1 = ptx::ex2(ptx::hi_f32(x));
+                        }
                         sum2[(c >> 1) & 3] = ptx::fadd2(sum2[(c >> 1) & 3], ptx::f32x2(p0, p1));
                         s[c >> 1] = __uint_as_float(ptx::pack_bf16x2(p0, p1));
                     }
