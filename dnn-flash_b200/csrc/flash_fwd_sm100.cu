@@ -1,6 +1,7 @@
 // flash_fwd_sm100.cu -- tiled attention forward for B200 (sm_100a).
 //
-// Persistent kernel: one CTA per SM walks a fixed sequence of work items (ItemSchedule).
+// Persistent kernel: one CTA per SM works through a sequence of work items (given out by a
+// counter in the workspace, or a fixed snake order without one).
 // An item is a PAIR of 128-row query tiles (Q0, Q1) of one (batch, q-head); the CTA
 // walks the KV tiles the tiling does not skip, loading each K/V tile once for both
 // query tiles.  The K/V ring, the barriers' phases and the TMEM allocation carry over
@@ -59,15 +60,21 @@ constexpr int kThreads = 384;  // three warpgroups
 constexpr int kWarpProducer = 8;
 constexpr int kWarpMma = 9;    // warps 10 and 11 only give their registers away
 // Register split: the kernel is compiled for kLaunchRegs per thread (three warps share an
-// SMSP); warpgroup 2 drops to kRegsCtrl and the two softmax warpgroups rise to
-// kRegsSoftmax, which must not exceed what the block was launched with.  The host checks
+// SMSP); warpgroup 2 drops to RegSplit::kCtrl and the two softmax warpgroups rise to
+// RegSplit::kSoftmax, which must not exceed what the block was launched with.  The host checks
 // the compiled register count before the first launch.
 constexpr int kLaunchRegs = 168;
-constexpr int kRegsCtrl = 104;
-constexpr int kRegsSoftmax = 200;
-static_assert(128 * kRegsCtrl + 256 * kRegsSoftmax <= kThreads * kLaunchRegs, "register split exceeds the launch");
-static_assert(kRegsCtrl % 8 == 0 && kRegsSoftmax % 8 == 0 && kRegsSoftmax <= 256, "setmaxnreg operands");
+// The split is per score-mod variant: the variants with the larger control code (both score
+// mods, or the bias tensor) need 112 registers there, the others keep 200 for the softmax.
+template <int MOD>
+struct RegSplit {
+    static constexpr int kCtrl = (MOD == 3 || MOD >= 4) ? 112 : 104;
+    static constexpr int kSoftmax = (MOD == 3 || MOD >= 4) ? 192 : 200;
+    static_assert(128 * kCtrl + 256 * kSoftmax <= kThreads * kLaunchRegs, "register split exceeds the launch");
+    static_assert(kCtrl % 8 == 0 && kSoftmax % 8 == 0 && kSoftmax <= 256, "setmaxnreg operands");
+};
 constexpr uint32_t kTmemCols = 512;
+constexpr int kItemQueue = 4;  // entries of the shared-memory queue of work items
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kChunkBytes = 128 * 128;  // 128 rows x 128 bytes (64 bf16)
 constexpr float kLog2e = 1.4426950408889634f;
@@ -86,9 +93,10 @@ struct Config {
     static constexpr uint32_t kTileBytes = 128 * D * 2;
     static constexpr uint32_t kOffSlots = 2 * kTileBytes;
     static constexpr uint32_t kOffBar = kOffSlots + kSlots * kTileBytes;
-    static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 2 + 2 + 1;
+    static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 2 + 2 + 2 * kItemQueue + 1;
     static constexpr uint32_t kOffRows = kOffBar + kNumBars * 8 + 16;  // after the barriers, TMEM slot, abort flag
-    static constexpr uint32_t kSmemBytes = kOffRows + 8 * 40 + 1024;     // + alignment slack
+    static constexpr uint32_t kOffQueue = kOffRows + 8 * 40;             // item queue (int64 x kItemQueue)
+    static constexpr uint32_t kSmemBytes = kOffQueue + 8 * kItemQueue + 1024;  // + alignment slack
     static constexpr uint32_t kTmemO = 256;
     // D = 64 leaves 128 TMEM columns free: P_i gets its own 64 columns at kTmemP + 64 i, so that
     // S_i(j+1) can be computed as soon as the softmax has loaded S_i(j) (instead of after
@@ -107,6 +115,8 @@ struct Bars {
     uint64_t* o_done;   // [2]
     uint64_t* s_free;   // [2] separate-P layout: the softmax has read S_i into registers
     uint64_t* pv_done;  // [2] separate-P layout: P_i.V has completed (P_i may be overwritten)
+    uint64_t* item_full;   // [kItemQueue] the producer wrote the queue entry
+    uint64_t* item_empty;  // [kItemQueue] the MMA thread and the 8 softmax warps read it
     uint64_t* drain;
 };
 
@@ -147,17 +157,37 @@ struct Item {
     bool valid1;       // Q1 has rows
 };
 
-// Item k covers query-tile pair n_pairs-1-k/(B Hq) of head k mod (B Hq): all heads of the
-// pair with the longest causal rows first.
+// Items come in blocks of units_per_block (batch, kv-head) units: inside a block, item i is
+// query-tile pair n_pairs-1-i/(U G) (longest causal rows first) of q-head i mod (U G) of the
+// block (G = q-heads per kv-head).  A block's K/V fits in L2 while its CTAs stream through it.
+// With one block holding every unit this is plain pair-major order over all heads.
 __device__ __forceinline__ Item decode_item(const FwdArgs& a, int64_t k) {
-    const int64_t n_bh = static_cast<int64_t>(a.batch) * a.heads_q;
-    const int64_t round = k / n_bh;
     Item I;
-    I.bh = static_cast<int>(k - round * n_bh);
-    I.pair = a.n_pairs - 1 - static_cast<int>(round);
-    I.b = I.bh / a.heads_q;
-    I.h = I.bh - I.b * a.heads_q;
-    I.hk = I.h / (a.heads_q / a.heads_kv);
+    const int64_t n_bh = static_cast<int64_t>(a.batch) * a.heads_q;
+    const int64_t n_units = static_cast<int64_t>(a.batch) * a.heads_kv;
+    if (a.units_per_block >= n_units) {  // one block: pair-major over all heads
+        const int64_t round = k / n_bh;
+        I.bh = static_cast<int>(k - round * n_bh);
+        I.pair = a.n_pairs - 1 - static_cast<int>(round);
+        I.b = I.bh / a.heads_q;
+        I.h = I.bh - I.b * a.heads_q;
+        I.hk = I.h / (a.heads_q / a.heads_kv);
+    } else {
+        const int64_t gq = a.heads_q / a.heads_kv;
+        const int64_t per_block = static_cast<int64_t>(a.units_per_block) * gq * a.n_pairs;
+        const int64_t blk = k / per_block;
+        const int64_t u0 = blk * a.units_per_block;
+        const int64_t row = min(static_cast<int64_t>(a.units_per_block), n_units - u0) * gq;  // items per pair
+        const int64_t i = k - blk * per_block;
+        const int64_t pr = i / row;
+        const int64_t j = i - pr * row;
+        const int64_t unit = u0 + j / gq;
+        I.pair = a.n_pairs - 1 - static_cast<int>(pr);
+        I.b = static_cast<int>(unit / a.heads_kv);
+        I.hk = static_cast<int>(unit - static_cast<int64_t>(I.b) * a.heads_kv);
+        I.h = I.hk * static_cast<int>(gq) + static_cast<int>(j - (j / gq) * gq);
+        I.bh = I.b * a.heads_q + I.h;
+    }
     I.q00 = I.pair * 2 * kTileQ;
     I.q01 = I.q00 + kTileQ;
     I.valid1 = I.q01 < a.m;
@@ -177,32 +207,18 @@ __device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, const Item& I, in
     return kv_entry(a, I.pair, j, I.valid1, I.qend0, I.qend1);
 }
 
-// Persistent schedule: the grid has G <= #SM CTAs and CTA c takes one item per round,
-// the c-th of round r when r is even and the (G-1-c)-th when r is odd.  Items are sorted by
-// decreasing causal work, so this snake order evens out long and short items the way the
-// hardware's greedy block scheduler would, and every role of the CTA derives the same
-// sequence without communicating.
-struct ItemSchedule {
-    int64_t n_items;
-    __device__ explicit ItemSchedule(const FwdArgs& a)
-        : n_items(static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs) {}
-    // Item index of this CTA's round `it`, or -1 once the CTA has no items left.
-    __device__ __forceinline__ int64_t item(int it) const {
-        const int64_t g = gridDim.x;
-        const int64_t c = (it & 1) ? (g - 1 - blockIdx.x) : blockIdx.x;
-        const int64_t k = static_cast<int64_t>(it) * g + c;
-        return k < n_items ? k : -1;
-    }
-    // Advances `it` to this CTA's next item that visits at least one KV tile.
-    __device__ __forceinline__ bool next_nonempty(const FwdArgs& a, int& it, Item& I) const {
-        for (;;) {
-            const int64_t k = item(++it);
-            if (k < 0) return false;
-            I = decode_item(a, k);
-            if (I.n_entries > 0) return true;
-        }
-    }
-};
+// Item assignment.  With a counter (args.sched) the producer warp of a CTA takes the next
+// item index whenever it starts a new item, so CTAs that finish early take more (greedy), and
+// publishes it through a small queue in shared memory that the MMA and softmax warps read.
+// Without one, CTA c takes one item per round of the grid, the c-th of round r when r is even
+// and the (G-1-c)-th when r is odd (items sorted by decreasing causal work: long and short
+// items even out), and every role computes that sequence itself.
+__device__ __forceinline__ int64_t static_item(int64_t n_items, int it) {
+    const int64_t g = gridDim.x;
+    const int64_t c = (it & 1) ? (g - 1 - blockIdx.x) : blockIdx.x;
+    const int64_t k = static_cast<int64_t>(it) * g + c;
+    return k < n_items ? k : -1;
+}
 
 // Bits of the 128 columns [k0, k0+128) that the BlockMask allows for query row qi
 // (attention.cpp:70-86; blocks outside the bitmap are disallowed).  Walks the few mask
@@ -317,13 +333,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars.o_done = bars.p_full + 2;
     bars.s_free = bars.o_done + 2;
     bars.pv_done = bars.s_free + 2;
-    bars.drain = bars.pv_done + 2;
+    bars.item_full = bars.pv_done + 2;
+    bars.item_empty = bars.item_full + kItemQueue;
+    bars.drain = bars.item_empty + kItemQueue;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars.drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const ItemSchedule sched(args);
+    const int64_t n_items = static_cast<int64_t>(args.batch) * args.heads_q * args.n_pairs;
+    // Greedy item assignment is compiled into the plain d = 128 kernel only (the shapes whose
+    // K/V outgrows L2 and whose speed depends on it); the other variants keep the fixed order.
+    constexpr bool kDyn = (MOD == 0 && D == 128);
+    volatile int64_t* item_q = reinterpret_cast<volatile int64_t*>(smem + Cfg::kOffQueue);
 
     if (threadIdx.x == 0) {
         ptx::mbar_init(bars.q_full, 1);
@@ -338,6 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&bars.o_done[i], 1);
             ptx::mbar_init(&bars.s_free[i], 128);
             ptx::mbar_init(&bars.pv_done[i], 1);
+        }
+        for (int i = 0; i < kItemQueue; ++i) {
+            ptx::mbar_init(&bars.item_full[i], 1);
+            ptx::mbar_init(&bars.item_empty[i], 9);
         }
         ptx::mbar_init(bars.drain, 1);
         *abort_flag = 0;
@@ -356,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp >= kWarpProducer) {
         // Warpgroup 2 (producer, MMA issuer, two idle warps) hands registers to the
         // softmax warpgroups; all four of its warps execute this one instruction.
-        ptx::setmaxnreg_dec<kRegsCtrl>();
+        ptx::setmaxnreg_dec<RegSplit<MOD>::kCtrl>();
         if (warp == kWarpProducer) {
             // ------------------------------------------------------------ TMA producer
             if (lane == 0) {
@@ -367,7 +393,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int q_loads = 0;
                 bool ok = true;
                 for (int it = 0; ok && !*abort_flag; ++it) {
-                    const int64_t k = sched.item(it);
+                    int64_t k;
+                    if (kDyn && args.sched) {
+                        // take the next item and publish it to the MMA and softmax warps (-1: none left)
+                        k = static_cast<int64_t>(atomicAdd(args.sched, 1ull));
+                        if (k >= n_items) k = -1;
+                        const int qs = it % kItemQueue;
+                        if (it >= kItemQueue &&
+                            !(ok = ptx::mbar_wait(&bars.item_empty[qs], ((it / kItemQueue) - 1) & 1, abort_flag,
+                                                  args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)))
+                            break;
+                        item_q[qs] = k;
+                        ptx::mbar_arrive(&bars.item_full[qs]);
+                    } else {
+                        k = static_item(n_items, it);  // every role computes the same sequence
+                    }
                     if (k < 0) break;
                     const Item I = decode_item(args, k);
                     if (I.n_entries == 0) continue;
@@ -493,9 +533,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                     return true;
                 };
 
+                // Advances `it` to the next item that visits a KV tile; false at the end of the
+                // sequence (or on a timeout, with ok cleared).
+                auto next_nonempty = [&](int& it, Item& In) -> bool {
+                    for (;;) {
+                        ++it;
+                        int64_t k;
+                        if (kDyn && args.sched) {
+                            const int qs = it % kItemQueue;
+                            if (!ptx::mbar_wait(&bars.item_full[qs], (it / kItemQueue) & 1, abort_flag, args.status,
+                                                ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)) {
+                                ok = false;
+                                return false;
+                            }
+                            k = item_q[qs];
+                            ptx::mbar_arrive(&bars.item_empty[qs]);
+                        } else {
+                            k = static_item(n_items, it);
+                        }
+                        if (k < 0) return false;
+                        In = decode_item(args, k);
+                        if (In.n_entries > 0) return true;
+                    }
+                };
+
                 int it = -1;
                 Item I;
-                const bool have = sched.next_nonempty(args, it, I);
+                const bool have = next_nonempty(it, I);
                 uint32_t e = have ? kv_entry(args, I, 0) : 0u;
                 if (have) ok = start_item(I, e, 0);
                 for (int j = 0, g = 0; have && ok; ++g) {
@@ -540,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ptx::tc_commit(&bars.slot_empty[tv % kSlots]);
                         if (acc[1]) ptx::tc_commit(&bars.o_done[1]);
                         acc[0] = acc[1] = false;
-                        if (!sched.next_nonempty(args, it, I)) break;
+                        if (!next_nonempty(it, I)) break;
                         e = kv_entry(args, I, 0);
                         j = 0;
                         if (!(ok = start_item(I, e, tk))) break;
@@ -563,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ softmax warps
-        ptx::setmaxnreg_inc<kRegsSoftmax>();
+        ptx::setmaxnreg_inc<RegSplit<MOD>::kSoftmax>();
         const int qtile = warp >> 2;         // 0: Q0, 1: Q1
         const int wq = warp & 3;             // TMEM lane quarter
         const int row = wq * 32 + lane;      // 0..127 == TMEM lane
@@ -583,7 +647,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const volatile RowItem* rec = rec_w;
 
         for (int it = 0; ok; ++it) {
-            const int64_t item = sched.item(it);
+            int64_t item;
+            if (kDyn && args.sched) {
+                item = -1;
+                if (lane == 0) {  // one reader per warp takes the item from the queue
+                    const int qs = it % kItemQueue;
+                    if (ptx::mbar_wait(&bars.item_full[qs], (it / kItemQueue) & 1, abort_flag, args.status,
+                                       ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)) {
+                        item = item_q[qs];
+                        ptx::mbar_arrive(&bars.item_empty[qs]);
+                    } else {
+                        item = -2;
+                    }
+                }
+                item = __shfl_sync(0xffffffffu, item, 0);
+                if (item == -2) {
+                    ok = false;
+                    break;
+                }
+            } else {
+                item = static_item(n_items, it);
+            }
             if (item < 0) break;
             __syncwarp();  // every lane is done with the previous record
             if (lane == 0) {
@@ -1041,13 +1125,13 @@ cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
 }  // namespace
 
 size_t workspace_bytes_for(int64_t seqlen_q, int64_t seqlen_k, bool has_mask) {
-    if (!has_mask) return 0;
+    if (!has_mask) return kSchedBytes;
     const int64_t n_qt = (seqlen_q + kTileQ - 1) / kTileQ;
     const int64_t n_pairs = (n_qt + 1) / 2;
     const int64_t n_kt = (seqlen_k + kTileK - 1) / kTileK;
     const size_t list = static_cast<size_t>(n_pairs * n_kt) * sizeof(uint32_t);
     const size_t count = static_cast<size_t>(n_pairs) * sizeof(int32_t);
-    return ((list + 255) & ~static_cast<size_t>(255)) + ((count + 255) & ~static_cast<size_t>(255));
+    return kSchedBytes + ((list + 255) & ~static_cast<size_t>(255)) + ((count + 255) & ~static_cast<size_t>(255));
 }
 
 int ensure_device_ready(int device, const char** err) {
@@ -1161,8 +1245,32 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
         *err = "cuTensorMapEncodeTiled rejected a Q/K/V layout (pointers and strides must be 16-byte aligned)";
         return ODF_ERR_INVALID_ARG;
     }
+    // Item assignment.  When the K/V of all (batch, kv-head) units exceeds what L2 keeps (about
+    // 32 MB of bf16 K and V per block) and a workspace is given, items come in blocks of units
+    // whose K/V fit, handed out greedily by a counter at the workspace's start (zeroed here), so
+    // the CTAs working at the same time share their K/V tiles in L2.  Otherwise (small K/V,
+    // block-mask lists whose uneven items want the global longest-first order, or no workspace)
+    // the fixed pair-major snake order, which needs no counter.
+    const int64_t n_units = static_cast<int64_t>(a.batch) * a.heads_kv;
+    a.sched = nullptr;
+    a.units_per_block = static_cast<int32_t>(n_units);
+    {
+        const int64_t kv_unit_bytes = 4 * static_cast<int64_t>(a.n) * L.head_dim;
+        int64_t per_block = (int64_t{32} << 20) / (kv_unit_bytes > 0 ? kv_unit_bytes : 1);
+        if (per_block < 1) per_block = 1;
+        if (per_block < n_units && a.mode != kModeList && L.workspace != nullptr &&
+            L.workspace_bytes >= kSchedBytes && L.head_dim == 128 && !L.has_alibi && !L.has_softcap &&
+            !L.has_bias) {  // the instantiation with greedy assignment compiled in
+            a.sched = static_cast<unsigned long long*>(L.workspace);
+            a.units_per_block = static_cast<int32_t>(per_block);
+            if (cudaMemsetAsync(L.workspace, 0, sizeof(unsigned long long), stream) != cudaSuccess) {
+                *err = "clearing the work-item counter failed";
+                return ODF_ERR_CUDA;
+            }
+        }
+    }
     if (a.mode == kModeList) {
-        uint8_t* ws = static_cast<uint8_t*>(L.workspace);
+        uint8_t* ws = static_cast<uint8_t*>(L.workspace) + kSchedBytes;
         const size_t list_bytes = static_cast<size_t>(a.n_pairs) * a.n_kt * sizeof(uint32_t);
         uint32_t* list = reinterpret_cast<uint32_t*>(ws);
         int32_t* count = reinterpret_cast<int32_t*>(ws + ((list_bytes + 255) & ~static_cast<size_t>(255)));

@@ -195,9 +195,12 @@ odf::FwdLaunch make_launch(const odf_fwd_params* p, const Resolved& r) {
 
 int run_device(const odf_fwd_params* p, const Resolved& r, cudaStream_t stream) {
     const size_t need = odf::workspace_bytes_for(p->seqlen_q, p->seqlen_k, p->block_mask != nullptr);
-    if (need > 0 && (p->workspace == nullptr || p->workspace_bytes < need))
+    if (p->block_mask != nullptr && p->workspace == nullptr)
         return fail(ODF_ERR_INVALID_ARG, "a block mask needs a device workspace of odf_fwd_workspace_size() bytes");
-    if (need > 0 && !aligned16(p->workspace)) return fail(ODF_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+    if (p->workspace != nullptr && p->workspace_bytes < need)
+        return fail(ODF_ERR_INVALID_ARG, "the workspace is smaller than odf_fwd_workspace_size() bytes");
+    if (p->workspace != nullptr && !aligned16(p->workspace))
+        return fail(ODF_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
     odf::FwdLaunch L = make_launch(p, r);
     const char* err = "";
     const int rc = odf::launch_flash_fwd(L, stream, &err);

@@ -51,7 +51,16 @@ struct FwdArgs {
     float alibi_slopes[ODF_MAX_EXPLICIT_SLOPES];
     const float* bias;          // same-shape additive bias, element strides below (0 = broadcast)
     int64_t bias_s0, bias_s1, bias_s2, bias_s3;
+    // Work items: blocks of units_per_block (batch, kv-head) units, the query-tile pairs of a
+    // block longest first.  sched != NULL: a zeroed 64-bit counter in the caller's workspace that
+    // hands items to CTAs as they become free; NULL: a fixed snake order (units_per_block is then
+    // every unit).
+    unsigned long long* sched;
+    int32_t units_per_block;
 };
+
+// The first kSchedBytes of a workspace hold the item counter; block-mask tile lists follow.
+constexpr size_t kSchedBytes = 256;
 
 // Validated, resolved launch request (device pointers only).
 struct FwdLaunch {

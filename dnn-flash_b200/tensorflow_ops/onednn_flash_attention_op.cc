@@ -180,6 +180,12 @@ public:
         p.k = ptr[1];
         p.v = ptr[2];
         p.qkv_dtype = ODF_DTYPE_BF16;
+        // workspace: the kernel's work-item counter (TensorFlow's allocator, 64-byte aligned)
+        Tensor ws;
+        const size_t wbytes = odf_fwd_workspace_size(&p);
+        OP_REQUIRES_OK(ctx, ctx->allocate_temp(DT_INT8, TensorShape({static_cast<int64_t>(wbytes)}), &ws));
+        p.workspace = const_cast<char*>(ws.tensor_data().data());
+        p.workspace_bytes = wbytes;
         OP_REQUIRES_OK(ctx, ToStatus(odf_flash_fwd_sm100(&p, stream), "device entry"));
     }
 };

@@ -75,7 +75,10 @@ typedef struct odf_fwd_params {
        ODF_BIAS_ALIBI = generated slopes 2^(-8 (h+1) / heads_q). */
     const float* alibi_slopes;
     float softcap;              /* > 0: s = softcap * tanh(s / softcap); 0 = off */
-    void* workspace;            /* device scratch of odf_fwd_workspace_size() bytes, or NULL if that is 0 */
+    void* workspace;            /* device scratch of odf_fwd_workspace_size() bytes (16-byte aligned): its first
+                                   256 bytes let the kernel hand work to SMs greedily, in L2-sized blocks
+                                   of heads (faster for long sequences); NULL = a fixed order, allowed
+                                   without a block mask */
     size_t workspace_bytes;
     /* Optional diagnostics (device, may be NULL): u8 [B*heads_q, q_tiles, kv_tiles],
        set to 1 for every 128x128 tile the kernel processes (never cleared by it). */
@@ -99,9 +102,9 @@ typedef struct odf_fwd_params {
  */
 int odf_flash_fwd_sm100(const odf_fwd_params* p, void* stream);
 
-/* Device scratch bytes odf_flash_fwd_sm100 needs for these params (0 unless a
-   block mask is given).  Plays the role of AttentionWorkspace::resize
-   (src/onednn_flash/attention_workspace.cpp:5-20). */
+/* Device scratch bytes for these params: 256 (the work-item counter, optional) plus,
+   with a block mask, the per-query-tile-pair KV lists (required).  Plays the role of
+   AttentionWorkspace::resize (src/onednn_flash/attention_workspace.cpp:5-20). */
 size_t odf_fwd_workspace_size(const odf_fwd_params* p);
 
 /* Capacity of the library-owned scratch used by odf_flash_fwd_sm100_noalloc. */
@@ -115,16 +118,17 @@ size_t odf_fwd_workspace_size(const odf_fwd_params* p);
  * allocator, a foreign-language binding with no allocator of its own).  The
  * caller still passes Q/K/V, O and LSE; p->workspace is ignored.
  *
- * Instead of a caller workspace, the block-mask tile lists go to a fixed array
- * of ODF_NOALLOC_SCRATCH_BYTES in this library's device memory (held by every
- * GPU that loads the library until the process exits).  Limit: the lists take
- * about ceil(seqlen_q/256) * ceil(seqlen_k/128) * 4 bytes; larger problems are
- * rejected with ODF_ERR_UNSUPPORTED.  Without a block mask no scratch is used.
- * The first call on a device looks up the array's device address (a one-time,
- * non-allocating runtime call); make that first call before any stream capture.
- * All calls share the one array and nothing in it needs to start at zero (each
- * launch rewrites the lists it reads), but calls that overlap on the GPU, on
- * different streams, race on it: serialise them.
+ * Instead of a caller workspace, a fixed array of ODF_NOALLOC_SCRATCH_BYTES in
+ * this library's device memory (held by every GPU that loads the library until
+ * the process exits) holds the work-item counter (256 bytes) and the block-mask
+ * tile lists.  Limit: the lists take about ceil(seqlen_q/256) *
+ * ceil(seqlen_k/128) * 4 bytes; larger problems are rejected with
+ * ODF_ERR_UNSUPPORTED.  The first call on a device looks up the array's device
+ * address (a one-time, non-allocating runtime call); make that first call
+ * before any stream capture.  All calls share the one array; each launch clears
+ * the counter and rewrites the lists it reads, so nothing else needs to start at
+ * zero, but calls that overlap on the GPU, on different streams, race on it:
+ * serialise them.
  * No counterpart in the reference (its workspace is always caller-owned).
  */
 int odf_flash_fwd_sm100_noalloc(const odf_fwd_params* p, void* stream);

@@ -80,7 +80,11 @@ def test_block_mask_needs_sizes_and_workspace():
     assert lib.odf_fwd_workspace_size(C.byref(p)) > 0
     assert lib.odf_flash_fwd_sm100(C.byref(p), None) == odf_b200.ODF_ERR_INVALID_ARG
     assert "workspace" in odf_b200.last_error()
-    assert lib.odf_fwd_workspace_size(C.byref(_params())) == 0
+    # without a mask the workspace only holds the work-item counter, and it stays optional
+    assert lib.odf_fwd_workspace_size(C.byref(_params())) == 256
+    small = _params(workspace=4096, workspace_bytes=64)
+    assert lib.odf_flash_fwd_sm100(C.byref(small), None) == odf_b200.ODF_ERR_INVALID_ARG
+    assert "smaller" in odf_b200.last_error()
 
 
 def test_misaligned_device_pointer_rejected():
