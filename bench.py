@@ -12,7 +12,7 @@ Ranks share nothing on the data path (heads are independent): the only
 collectives are the barrier and the max-over-ranks of the timed region.
 
 Usage:
-  python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--config c1..c5]
+  python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--config c1..c5|mha8k_causal|mha8k_dense]
   torchrun --nproc-per-node N bench.py --gpus N ...
 """
 from __future__ import annotations
@@ -45,6 +45,12 @@ CONFIGS = {
                out="bf16", mask="window4_prefix4"),
     "c5": dict(B=1, Hq=64, Hkv=8, N=32768, D=128, causal=True, alibi=False, softcap=0.0, in_scale=1.0,
                out="bf16", mask=None),
+    # Not BASELINE configs: the north-star shape (causal N=8192, d=128) as multi-head attention,
+    # causal and dense, used to profile the kernel's K/V reuse in L2 (no GQA sharing of K/V).
+    "mha8k_causal": dict(B=2, Hq=32, Hkv=32, N=8192, D=128, causal=True, alibi=False, softcap=0.0,
+                         in_scale=1.0, out="bf16", mask=None),
+    "mha8k_dense": dict(B=2, Hq=32, Hkv=32, N=8192, D=128, causal=False, alibi=False, softcap=0.0,
+                        in_scale=1.0, out="bf16", mask=None),
 }
 WORKLOAD_NAMES = {
     "c1": "c1_mha_noncausal_b1h4_n512_d64",
@@ -52,6 +58,8 @@ WORKLOAD_NAMES = {
     "c3": "c3_causal_alibi_softcap50_b2h32_n8192_d128",
     "c4": "c4_block_sparse_window512_prefix4_b8h16_n4096_d128",
     "c5": "c5_gqa_causal_hq64_hkv8_n32768_d128",
+    "mha8k_causal": "mha_causal_b2h32_n8192_d128",
+    "mha8k_dense": "mha_dense_b2h32_n8192_d128",
 }
 
 
@@ -95,9 +103,12 @@ def measured_peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def profiled_traffic(workload):
-    """DRAM bytes per launch from the committed ncu summary of this kernel/workload, if any."""
-    path = ROOT / "profiles" / f"flash_fwd_{workload.split('_')[0]}.md"
+def profiled_traffic(config, seq_len=None):
+    """DRAM bytes per launch from the committed ncu summary of this kernel/config, if any
+    (profiles/flash_fwd_<config>.md; none for a --seq-len override)."""
+    if seq_len is not None:
+        return None
+    path = ROOT / "profiles" / f"flash_fwd_{config}.md"
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
@@ -420,7 +431,7 @@ def run_ours(args, cfg, workload):
                 "frac": achieved / peak,
                 "peak_kind": f"{peak_kind} bf16 burst (cuBLAS); sustained {peak_sus}",
                 "frac_of_sustained": achieved / peak_sus,
-                "traffic": profiled_traffic(workload),
+                "traffic": profiled_traffic(args.config, args.seq_len),
                 "kernel": "flash_fwd_kernel<128,0>",
                 "avg_launch_ms": avg_launch_ms,
             },
