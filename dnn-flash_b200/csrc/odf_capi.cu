@@ -210,11 +210,17 @@ int run_device(const odf_fwd_params* p, const Resolved& r, cudaStream_t stream) 
 
 // ------------------------------------------------------------------ host entry
 // Device buffers of the host entry, per thread and device, grown on demand.
+// Three stages run on their own streams -- copy in (and fp32 -> bf16), the kernel, copy out --
+// over kHostSets rotating buffer sets, so chunk c's upload, chunk c-1's kernel and chunk c-2's
+// download overlap.  Events order a stage after the previous stage of its chunk and a buffer
+// set's reuse after the last stage that read it.
+constexpr int kHostSets = 3;
 struct HostPool {
     int device = -1;
-    cudaStream_t streams[2] = {nullptr, nullptr};
-    void* buf[2][8] = {};
-    size_t cap[2][8] = {};
+    cudaStream_t streams[3] = {nullptr, nullptr, nullptr};  // copy in, compute, copy out
+    cudaEvent_t in_done[kHostSets] = {}, comp_done[kHostSets] = {}, out_done[kHostSets] = {};
+    void* buf[kHostSets][8] = {};
+    size_t cap[kHostSets][8] = {};
     void* mask = nullptr;
     size_t mask_cap = 0;
     ~HostPool() {
@@ -223,6 +229,9 @@ struct HostPool {
             for (void*& b : set)
                 if (b) cudaFree(b);
         if (mask) cudaFree(mask);
+        for (auto* evs : {in_done, comp_done, out_done})
+            for (int i = 0; i < kHostSets; ++i)
+                if (evs[i]) cudaEventDestroy(evs[i]);
         for (auto& s : streams)
             if (s) cudaStreamDestroy(s);
     }
@@ -275,7 +284,11 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
     cudaError_t e = cudaSuccess;
     for (auto& s : pool.streams)
         if (!s && e == cudaSuccess) e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    for (auto* evs : {pool.in_done, pool.comp_done, pool.out_done})
+        for (int i = 0; i < kHostSets; ++i)
+            if (!evs[i] && e == cudaSuccess) e = cudaEventCreateWithFlags(&evs[i], cudaEventDisableTiming);
     if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+    cudaStream_t s_in = pool.streams[0], s_comp = pool.streams[1], s_out = pool.streams[2];
 
     // Work is chunked over (batch, kv-head) units; a unit's Q/O rows (its
     // heads_q/heads_kv query heads) and K/V rows are contiguous.
@@ -314,8 +327,8 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         const int64_t u1 = std::min(units, u0 + per);
         if (u0 >= u1) break;
         const int64_t cu = u1 - u0;
-        const int slot = static_cast<int>(c & 1);
-        cudaStream_t st = pool.streams[slot];
+        const int slot = static_cast<int>(c % kHostSets);
+        cudaStream_t st = s_in;  // this chunk's copies and conversions
         void *dq, *dk, *dv, *dout, *dlse = nullptr, *dstage = nullptr, *dws = nullptr;
         if ((e = pool.reserve(slot, 0, cu * q_unit * 2, &dq)) != cudaSuccess ||
             (e = pool.reserve(slot, 1, cu * kv_unit * 2, &dk)) != cudaSuccess ||
@@ -328,6 +341,9 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
             (e = pool.reserve(slot, 5, cu * std::max(q_unit, std::max(kv_unit, v_unit)) * 4, &dstage)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
         if (ws_bytes && (e = pool.reserve(slot, 6, ws_bytes, &dws)) != cudaSuccess)
+            return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+        // the set's inputs are rewritten once the kernel of chunk c - kHostSets has read them
+        if (c >= kHostSets && (e = cudaStreamWaitEvent(s_in, pool.comp_done[slot], 0)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
         // Same-shape bias: the footprint of each (batch, q-head) plane of this chunk, copied to a
         // device staging buffer with the row/key strides kept (one plane when the bias is
@@ -371,6 +387,8 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
             }
             if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
         }
+        if ((e = cudaEventRecord(pool.in_done[slot], s_in)) != cudaSuccess)
+            return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
         odf_fwd_params sub = *p;
         sub.q = dq;
         sub.k = dk;
@@ -407,12 +425,22 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         Resolved rs;
         rc = validate(&sub, false, &rs);
         if (rc != ODF_OK) return rc;
-        rc = run_device(&sub, rs, st);
+        // kernel: after this chunk's copies, and after chunk c - kHostSets's outputs left the set
+        e = cudaStreamWaitEvent(s_comp, pool.in_done[slot], 0);
+        if (e == cudaSuccess && c >= kHostSets) e = cudaStreamWaitEvent(s_comp, pool.out_done[slot], 0);
+        if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+        rc = run_device(&sub, rs, s_comp);
         if (rc != ODF_OK) return rc;
-        e = cudaMemcpyAsync(static_cast<char*>(p->o) + u0 * o_unit * out_es, dout, cu * o_unit * out_es,
-                            cudaMemcpyDeviceToHost, st);
+        if ((e = cudaEventRecord(pool.comp_done[slot], s_comp)) != cudaSuccess)
+            return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+        // copy out after the kernel
+        e = cudaStreamWaitEvent(s_out, pool.comp_done[slot], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(static_cast<char*>(p->o) + u0 * o_unit * out_es, dout, cu * o_unit * out_es,
+                                cudaMemcpyDeviceToHost, s_out);
         if (e == cudaSuccess && p->lse)
-            e = cudaMemcpyAsync(p->lse + u0 * G * M, dlse, cu * G * M * sizeof(float), cudaMemcpyDeviceToHost, st);
+            e = cudaMemcpyAsync(p->lse + u0 * G * M, dlse, cu * G * M * sizeof(float), cudaMemcpyDeviceToHost, s_out);
+        if (e == cudaSuccess) e = cudaEventRecord(pool.out_done[slot], s_out);
         if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
     }
     for (auto& s : pool.streams) {
