@@ -96,7 +96,11 @@ struct Config {
     static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 2 + 2 + 2 * kItemQueue + 1;
     static constexpr uint32_t kOffRows = kOffBar + kNumBars * 8 + 16;  // after the barriers, TMEM slot, abort flag
     static constexpr uint32_t kOffQueue = kOffRows + 8 * 40;             // item queue (int64 x kItemQueue)
-    static constexpr uint32_t kSmemBytes = kOffQueue + 8 * kItemQueue + 1024;  // + alignment slack
+    // same-shape bias: 2 KB per softmax warp to transpose coalesced row reads (32 rows x 16 keys)
+    static constexpr uint32_t kOffBias = (kOffQueue + 8 * kItemQueue + 127) & ~127u;  // float4 stores
+    static_assert(kOffBias % 16 == 0 && kOffRows % 8 == 0 && kOffQueue % 8 == 0, "shared-memory alignment");
+    static constexpr uint32_t kSmemBytes = kOffBias + 8 * 32 * 16 * 4 + 1024;  // + alignment slack
+    static_assert(kSmemBytes <= 232448, "shared memory per block");
     static constexpr uint32_t kTmemO = 256;
     // D = 64 leaves 128 TMEM columns free: P_i gets its own 64 columns at kTmemP + 64 i, so that
     // S_i(j+1) can be computed as soon as the softmax has loaded S_i(j) (instead of after
@@ -753,7 +757,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int ncols = (qi < args.m) ? min(kTileK, args.n - k0) : 0;
                     const float* brow = args.bias + rec->bias_off + static_cast<int64_t>(qi) * args.bias_s2 +
                                         static_cast<int64_t>(k0) * args.bias_s3;
-                    if (ncols == kTileK && args.bias_s3 == 1 && (reinterpret_cast<uintptr_t>(brow) & 15u) == 0) {
+                    const bool vec_row =
+                        ncols == kTileK && args.bias_s3 == 1 && (reinterpret_cast<uintptr_t>(brow) & 15u) == 0;
+                    if (__all_sync(0xffffffffu, vec_row)) {
+                        // The warp's 32 rows are whole, key-contiguous and aligned: each load reads 8
+                        // rows x 64 bytes (a thread owning a row would touch 32 lines per load); the
+                        // rows are turned around, 16 keys at a time, through 2 KB of the warp's shared
+                        // memory, whose 16-byte units are XOR-swizzled by row so the row reads are
+                        // conflict-free.
+                        float* stage = reinterpret_cast<float*>(smem + Cfg::kOffBias) + warp * (32 * 16);
+                        const float* wrow0 = brow - static_cast<int64_t>(lane) * args.bias_s2;  // warp's row 0
+#pragma unroll
+                        for (int ch = 0; ch < kTileK / 16; ++ch) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const int r = 8 * i + (lane >> 2);
+                                const float4 v = __ldg(reinterpret_cast<const float4*>(
+                                                           wrow0 + static_cast<int64_t>(r) * args.bias_s2 + ch * 16) +
+                                                       (lane & 3));
+                                reinterpret_cast<float4*>(stage + r * 16)[(lane & 3) ^ ((r >> 1) & 3)] = v;
+                            }
+                            __syncwarp();
+#pragma unroll
+                            for (int c4 = 0; c4 < 4; ++c4) {
+                                const float4 bv =
+                                    reinterpret_cast<const float4*>(stage + lane * 16)[c4 ^ ((lane >> 1) & 3)];
+                                const int c = ch * 16 + 4 * c4;
+                                s[c + 0] = fmaf(s[c + 0], mul, bv.x * bmul);
+                                s[c + 1] = fmaf(s[c + 1], mul, bv.y * bmul);
+                                s[c + 2] = fmaf(s[c + 2], mul, bv.z * bmul);
+                                s[c + 3] = fmaf(s[c + 3], mul, bv.w * bmul);
+                            }
+                            __syncwarp();
+                        }
+                    } else if (vec_row) {
                         const float4* b4 = reinterpret_cast<const float4*>(brow);
 #pragma unroll
                         for (int c4 = 0; c4 < kTileK / 4; ++c4) {
