@@ -339,6 +339,14 @@ def run_ours(args, cfg, workload):
         odf_b200.flash_fwd(q, k, v, causal=cfg["causal"], alibi=cfg["alibi"], softcap=cfg["softcap"],
                            block_mask=mask, out=o, lse_out=lse)
 
+    # algorithmic bytes: Q, K, V read once, O and LSE written once
+    out_es = 2 if out_dtype == torch.bfloat16 else 4
+    alg_bytes = (B * Hq * N * D * 2 + 2 * B * Hkv * N * D * 2 + B * Hq * N * D * out_es + B * Hq * N * 4)
+    # Working sets under twice the 126 MB L2 get an L2 flush (a 256 MB write) between timed steps;
+    # the value then sums the per-step event times, which exclude the flushes.
+    l2_bytes = 126 * 2 ** 20
+    flush = torch.empty(64 * 2 ** 20, dtype=torch.float32, device=dev) if alg_bytes < 2 * l2_bytes else None
+
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
@@ -353,6 +361,8 @@ def run_ours(args, cfg, workload):
     with ClockSampler(local) as clocks:
         t_begin.record(stream)
         for i in range(args.steps):
+            if flush is not None:
+                flush.zero_()
             starts[i].record(stream)
             step()
             ends[i].record(stream)
@@ -361,8 +371,8 @@ def run_ours(args, cfg, workload):
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    total_ms = t_begin.elapsed_time(t_end)
     per_launch_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    total_ms = sum(per_launch_ms) if flush is not None else t_begin.elapsed_time(t_end)
     status = odf_b200.device_status()
     if status != 0:
         raise RuntimeError(f"device status {status}: an in-kernel wait timed out")
@@ -398,6 +408,19 @@ def run_ours(args, cfg, workload):
     value = world * flop_rank * args.steps / (total_ms * 1e-3) / 1e12  # every rank runs the same FLOP
     avg_launch_ms = statistics.mean(per_launch_ms)
     achieved = flop_rank / (avg_launch_ms * 1e-3) / 1e12
+    mod = (1 if cfg["alibi"] else 0) | (2 if cfg["softcap"] > 0 else 0)
+    if flop_rank / alg_bytes >= peak * 1e12 / (hbm * 1e9):  # above the ridge point: tensor-bound
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_kind": f"{peak_kind} bf16 burst (cuBLAS); sustained {peak_sus}",
+                "frac_of_sustained": achieved / peak_sus}
+    else:  # below it (short, small shapes): algorithmic bytes against the measured copy bandwidth
+        gbs = alg_bytes / (avg_launch_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                "peak_kind": f"{peak_kind} HBM copy bandwidth", "tflops": achieved}
+    roof.update({"traffic": profiled_traffic(args.config, args.seq_len), "algorithmic_bytes": alg_bytes,
+                 "kernel": f"flash_fwd_kernel<{D},{mod}>", "avg_launch_ms": avg_launch_ms})
+    l2_note = ("L2 flushed (256 MB write) between timed steps; value from per-step events" if flush is not None
+               else f"inputs and outputs ({alg_bytes / 2 ** 20:.0f} MiB) larger than twice L2; no flush needed")
     result = None
     if rank == 0:
         result = {
@@ -421,20 +444,9 @@ def run_ours(args, cfg, workload):
                 "block_mask": cfg["mask"], "out_dtype": cfg["out"], "lse": True,
                 "parallelism": f"(batch x head) shards, {world} GPU(s), no collective on the data path",
                 "flop_per_gpu_step": flop_rank,
-                "l2": "inputs larger than L2 (Q 512 MiB, K/V 128 MiB, O 512 MiB); no flush needed",
+                "l2": l2_note,
             },
-            "roofline": {
-                "bound": "tensor",
-                "achieved": achieved,
-                "peak": peak,
-                "unit": "TFLOP/s",
-                "frac": achieved / peak,
-                "peak_kind": f"{peak_kind} bf16 burst (cuBLAS); sustained {peak_sus}",
-                "frac_of_sustained": achieved / peak_sus,
-                "traffic": profiled_traffic(args.config, args.seq_len),
-                "kernel": "flash_fwd_kernel<128,0>",
-                "avg_launch_ms": avg_launch_ms,
-            },
+            "roofline": roof,
             "e2e": {"value": world * flop_rank / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "path": "odf_flash_fwd_host (pinned host buffers)"},
             "gpu_launches": args.steps * launches_per_step,
