@@ -61,6 +61,14 @@ def test_validation_codes(field, value, code):
     assert odf_b200.last_error()
 
 
+def test_explicit_alibi_slopes_limited_to_256_heads():
+    lib = odf_b200.load_library()
+    slopes = (C.c_float * 300)()
+    p = _params(bias_kind=odf_b200.ODF_BIAS_ALIBI, heads_q=300, heads_kv=300, alibi_slopes=C.cast(slopes, C.c_void_p))
+    assert lib.odf_flash_fwd_sm100(C.byref(p), None) == odf_b200.ODF_ERR_UNSUPPORTED
+    assert "256" in odf_b200.last_error()
+
+
 def test_same_shape_bias_checks():
     lib = odf_b200.load_library()
     p = _params(bias_kind=odf_b200.ODF_BIAS_SAME_SHAPE, bias=4096)

@@ -184,6 +184,19 @@ def test_score_mods(alibi, softcap):
     check_close(o, lse, o_ref, lse_ref, f"alibi={alibi} softcap={softcap}")
 
 
+@pytest.mark.parametrize("softcap", [0.0, 30.0])
+def test_generated_alibi_slopes_beyond_256_heads(softcap):
+    """Up to 256 heads the host evaluates the generated slopes 2^(-8(h+1)/H) into the launch;
+    beyond that the kernel evaluates them itself.  320 q-heads over 40 kv-heads (GQA 8)."""
+    import oracle
+
+    H, Hk = 320, 40
+    q, k, v = make_qkv(41, 1, H, Hk, 200, 200, 64)
+    o, lse = run_gpu(q, k, v, causal=True, alibi=True, softcap=softcap)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, alibi_slopes=oracle.alibi_slopes(H), softcap=softcap)
+    check_close(o, lse, o_ref, lse_ref, f"generated slopes, 320 heads, softcap {softcap}")
+
+
 def test_explicit_alibi_slopes_and_noncausal_scale():
     H = 3
     slopes = np.array([0.5, 0.03125, 0.25], dtype=np.float32)
