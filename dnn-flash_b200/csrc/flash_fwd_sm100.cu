@@ -959,9 +959,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int qi = rec->q0 + row;
                 const bool valid_row = qi < args.m;
                 const float inv_l = (l_run > 0.0f) ? (1.0f / l_run) : 0.0f;
-                const int64_t orow = static_cast<int64_t>(b) * args.o_stride_b +
-                                     static_cast<int64_t>(h) * args.o_stride_h +
-                                     static_cast<int64_t>(qi) * args.o_stride_t;
+                // O leaves through the warp's 2 KB of shared memory (16-byte units XOR-swizzled by
+                // row, conflict-free both ways): a thread owning a row would write 32 rows x 16 B
+                // per store; read back, each store writes 8 rows x 64 contiguous bytes.
+                const int qw = rec->q0 + wq * 32;  // the warp's first row
+                const int64_t obase = static_cast<int64_t>(b) * args.o_stride_b +
+                                      static_cast<int64_t>(h) * args.o_stride_h +
+                                      static_cast<int64_t>(qw) * args.o_stride_t;
+                uint4* srow = reinterpret_cast<uint4*>(smem + Cfg::kOffBias) + warp * (32 * 4) + lane * 4;
+                const uint4* sbase = reinterpret_cast<const uint4*>(smem + Cfg::kOffBias) + warp * (32 * 4);
+                const int wsw = (lane >> 1) & 3;  // swizzle of this thread's staging row
 #pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
                     float o[32];
@@ -971,26 +978,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int t = 0; t < 32; ++t) o[t] = 0.0f;
                     }
-                    if (valid_row) {
-                        if (args.o_bf16) {
-                            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(args.o) + orow + c * 32);
+                    // bf16: the 32 columns are one 64-byte piece per row; fp32: two 16-column pieces
 #pragma unroll
-                            for (int v = 0; v < 4; ++v) {
-                                uint4 w;
+                    for (int hf = 0; hf < 2; ++hf) {
+                        if (args.o_bf16 && hf == 1) break;
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            uint4 w;
+                            if (args.o_bf16) {
                                 w.x = ptx::pack_bf16x2(o[8 * v + 0] * inv_l, o[8 * v + 1] * inv_l);
                                 w.y = ptx::pack_bf16x2(o[8 * v + 2] * inv_l, o[8 * v + 3] * inv_l);
                                 w.z = ptx::pack_bf16x2(o[8 * v + 4] * inv_l, o[8 * v + 5] * inv_l);
                                 w.w = ptx::pack_bf16x2(o[8 * v + 6] * inv_l, o[8 * v + 7] * inv_l);
-                                dst[v] = w;
+                            } else {
+                                const int t = 16 * hf + 4 * v;
+                                w = make_uint4(__float_as_uint(o[t + 0] * inv_l), __float_as_uint(o[t + 1] * inv_l),
+                                               __float_as_uint(o[t + 2] * inv_l), __float_as_uint(o[t + 3] * inv_l));
                             }
-                        } else {
-                            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(args.o) + orow + c * 32);
+                            srow[v ^ wsw] = w;
+                        }
+                        __syncwarp();
 #pragma unroll
-                            for (int v = 0; v < 8; ++v) {
-                                dst[v] = make_float4(o[4 * v + 0] * inv_l, o[4 * v + 1] * inv_l, o[4 * v + 2] * inv_l,
-                                                     o[4 * v + 3] * inv_l);
+                        for (int i = 0; i < 4; ++i) {
+                            const int r = 8 * i + (lane >> 2);
+                            const int u = lane & 3;
+                            const uint4 w = sbase[r * 4 + (u ^ ((r >> 1) & 3))];
+                            if (qw + r < args.m) {
+                                const int64_t off = obase + static_cast<int64_t>(r) * args.o_stride_t;
+                                if (args.o_bf16) {
+                                    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(args.o) + off + c * 32 +
+                                                              u * 8) = w;
+                                } else {
+                                    *reinterpret_cast<uint4*>(static_cast<float*>(args.o) + off + c * 32 + hf * 16 +
+                                                              u * 4) = w;
+                                }
                             }
                         }
+                        __syncwarp();
                     }
                 }
                 if (valid_row && args.lse) {
