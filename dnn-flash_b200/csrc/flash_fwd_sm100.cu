@@ -285,33 +285,16 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
 template <int D>
 __host__ __device__ constexpr uint32_t poly_exp2_mask() { return D == 64 ? ODF_POLY_MASK_D64 : 0u; }
 
-// Reciprocal of a pair d in (1, 2] on the FMA pipe: integer-subtraction seed (constant
-// fitted here for <= 5.1% relative error) and three Newton steps r <- r (2 - d r) (~1.5e-7).
-__device__ __forceinline__ uint64_t rcp2_1to2(uint64_t d) {
-    const uint32_t lo = 0x7ef311c2u - static_cast<uint32_t>(d);
-    const uint32_t hi = 0x7ef311c2u - static_cast<uint32_t>(d >> 32);
-    uint64_t r = (static_cast<uint64_t>(hi) << 32) | lo;
-    const uint64_t two = ptx::f32x2(2.0f);
-    const uint64_t neg_d = d ^ 0x8000000080000000ull;
-#pragma unroll
-    for (int it = 0; it < 3; ++it) r = ptx::fmul2(r, ptx::ffma2(neg_d, r, two));
-    return r;
-}
-
-// softcap * tanh(x / softcap) * log2(e) for a pair of scores, from
-// tanh|t| = (1 - e) / (1 + e) with e = 2^(-2 log2(e) |t|) in (0, 1]: one MUFU ex2 per score,
-// the division on the FMA pipe, no overflow for any |t|, and the sign restored from x.
-// Absolute error a few fp32 ulps of 1 (softcap * tanh within ~1e-5 of the fp32 value).
-__device__ __forceinline__ uint64_t softcap2(uint64_t x, uint64_t k2, uint64_t cap_log2) {
-    const uint64_t u = ptx::fmul2(x, k2);  // 2 log2(e) t
+// softcap * tanh(t) * log2(e) for a pair of scores given u = 2 log2(e) t (t = score / softcap),
+// from tanh|t| = 2 / (1 + e) - 1 with e = 2^(-|u|) in (0, 1]: two MUFU operations per score (ex2
+// and the reciprocal, both within a few ulps), no overflow for any |t|, the scale folded into one
+// FMA and the sign restored from u.  Absolute error a few fp32 ulps of softcap * log2(e).
+__device__ __forceinline__ uint64_t softcap2(uint64_t u, uint64_t cap2x, uint64_t neg_cap) {
     const float e0 = ptx::ex2(-fabsf(ptx::lo_f32(u)));
     const float e1 = ptx::ex2(-fabsf(ptx::hi_f32(u)));
-    const uint64_t e = ptx::f32x2(e0, e1);
-    const uint64_t one = ptx::f32x2(1.0f);
-    const uint64_t den = ptx::fadd2(e, one);
-    const uint64_t num = ptx::ffma2(e, ptx::f32x2(-1.0f), one);
-    const uint64_t th = ptx::fmul2(num, rcp2_1to2(den)) | (x & 0x8000000080000000ull);
-    return ptx::fmul2(th, cap_log2);
+    const uint64_t den = ptx::fadd2(ptx::f32x2(e0, e1), ptx::f32x2(1.0f));
+    const uint64_t r = ptx::f32x2(ptx::rcp(ptx::lo_f32(den)), ptx::rcp(ptx::hi_f32(den)));
+    return ptx::ffma2(r, cap2x, neg_cap) ^ (u & 0x8000000080000000ull);
 }
 
 template <int D, int MOD>
@@ -815,11 +798,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (MOD & kModSoftcap) {
                     const float base = static_cast<float>(k0 - qi);
-                    const uint64_t scale2 = ptx::f32x2(args.scale);
-                    const uint64_t slope2 = ptx::f32x2(slope);
-                    const uint64_t sb2 = ptx::f32x2(slope * base);
-                    const uint64_t k2 = ptx::f32x2(2.0f * kLog2e * args.inv_softcap);
-                    const uint64_t cap_log2 = ptx::f32x2(args.softcap * kLog2e);
+                    // u = (s * scale + ALiBi) * 2 log2(e) / softcap, the soft-cap's argument
+                    const float kSoftcapU = 2.0f * kLog2e * args.inv_softcap;
+                    const uint64_t scale2 = ptx::f32x2(args.scale * kSoftcapU);
+                    const uint64_t slope2 = ptx::f32x2(slope * kSoftcapU);
+                    const uint64_t sb2 = ptx::f32x2(slope * base * kSoftcapU);
+                    const uint64_t cap2x = ptx::f32x2(2.0f * args.softcap * kLog2e);
+                    const uint64_t neg_cap = ptx::f32x2(-args.softcap * kLog2e);
 #pragma unroll
                     for (int c = 0; c < 128; c += 2) {
                         uint64_t x = ptx::f32x2(s[c], s[c + 1]);
@@ -827,10 +812,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint64_t bias = ptx::ffma2(ptx::f32x2(static_cast<float>(c), static_cast<float>(c + 1)),
                                                              slope2, sb2);
                             x = ptx::ffma2(x, scale2, bias);
-                        } else if (!(MOD & kModBias)) {  // the bias pass already scaled
+                        } else if (MOD & kModBias) {  // the bias pass left s * scale + bias
+                            x = ptx::fmul2(x, ptx::f32x2(kSoftcapU));
+                        } else {
                             x = ptx::fmul2(x, scale2);
                         }
-                        const uint64_t y = softcap2(x, k2, cap_log2);
+                        const uint64_t y = softcap2(x, cap2x, neg_cap);
                         s[c] = ptx::lo_f32(y);
                         s[c + 1] = ptx::hi_f32(y);
                     }
