@@ -64,11 +64,15 @@ WORKLOAD_NAMES = {
 
 
 def block_mask_for(cfg):
+    """The c4 workload's 128x128 block mask: allowed(qb, kb) = kb <= qb and (qb - kb < 4 or kb < 4)
+    (a 512-token sliding window plus 4 global prefix blocks), u8 row-major, nonzero = allowed."""
     if cfg["mask"] is None:
         return None
-    import oracle
+    import numpy as np
 
-    return oracle.sliding_window_prefix_mask(cfg["N"] // 128, 4, 4)
+    qb = np.arange(cfg["N"] // 128)[:, None]
+    kb = np.arange(cfg["N"] // 128)[None, :]
+    return ((kb <= qb) & ((qb - kb < 4) | (kb < 4))).astype(np.uint8)
 
 
 def flop_per_unit_pairs(cfg):
