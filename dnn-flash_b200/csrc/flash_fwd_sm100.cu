@@ -841,13 +841,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (ragged || diag || bitmap) {
                     int limit = args.n - 1 - k0;
                     if (args.causal) limit = min(limit, qi - k0);
-                    const uint4 allow = bitmap ? row_allow_bits(args, qi, k0)
-                                               : make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+                    if (!bitmap) {  // the tile's entry is the same for the whole warp
 #pragma unroll
-                    for (int c = 0; c < 128; ++c) {
-                        const uint32_t word = (c < 32) ? allow.x : (c < 64) ? allow.y : (c < 96) ? allow.z : allow.w;
-                        const bool keep = (c <= limit) && ((word >> (c & 31)) & 1u);
-                        s[c] = keep ? s[c] : -INFINITY;
+                        for (int c = 0; c < 128; ++c) s[c] = (c <= limit) ? s[c] : -INFINITY;
+                    } else {
+                        const uint4 allow = row_allow_bits(args, qi, k0);
+#pragma unroll
+                        for (int c = 0; c < 128; ++c) {
+                            const uint32_t word = (c < 32) ? allow.x : (c < 64) ? allow.y : (c < 96) ? allow.z : allow.w;
+                            const bool keep = (c <= limit) && ((word >> (c & 31)) & 1u);
+                            s[c] = keep ? s[c] : -INFINITY;
+                        }
                     }
                 }
 
