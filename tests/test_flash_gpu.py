@@ -223,6 +223,29 @@ def test_strided_bmhd_layout_and_bf16_output():
     check_close(o.float().cpu().numpy(), lse.cpu().numpy(), o_ref, lse_ref, "strided")
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("o_dtype", ["float32", "bfloat16"])
+def test_output_writes_stay_inside_o(d, o_dtype):
+    """O is a view into a larger buffer (rows past M, columns past D): the padding keeps its
+    sentinel, so the epilogue writes exactly rows < M and columns < D of every (batch, head)."""
+    torch = _torch()
+    import odf_b200
+
+    B, H, M = 2, 3, 300
+    dt = getattr(torch, o_dtype)
+    q, k, v = make_qkv(31 + d, B, H, H, M, M, d)
+    big = torch.full((B, H, M + 70, d + 24), -7.0, dtype=dt, device="cuda")
+    out = big[:, :, :M, :d]
+    o, lse = odf_b200.flash_fwd(to_dev(q), to_dev(k), to_dev(v), causal=True, out=out)
+    torch.cuda.synchronize()
+    assert o.data_ptr() == out.data_ptr()
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True)
+    check_close(out.float().cpu().numpy(), lse.cpu().numpy(), o_ref, lse_ref, f"padded O {o_dtype} d={d}")
+    pad = big.float().cpu().numpy()
+    assert np.all(pad[:, :, M:, :] == -7.0), "rows past M were written"
+    assert np.all(pad[:, :, :, d:] == -7.0), "columns past D were written"
+
+
 # --------------------------------------------------------------------------- skip set
 @pytest.mark.parametrize("case", ["causal", "mask", "mask_causal", "ragged"])
 def test_skip_set_bit_exact(case):
