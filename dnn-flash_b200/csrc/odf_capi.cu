@@ -299,10 +299,28 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
     int64_t n_chunks = std::min<int64_t>(units, 8);
     while (n_chunks > 1 && (units / n_chunks) * G * n_qt < 2 * 148) --n_chunks;
     const int64_t per = (units + n_chunks - 1) / n_chunks;
+    // A chunk is units [u0, u0 + cu) with all their query heads, or query heads [g0, g0 + ng)
+    // of the single unit u0.  Only the first chunk's upload and the last chunk's download run
+    // alone, so with a pipeline of four or more chunks the first and the last unit are split:
+    // a quarter of their query heads (at least one) goes first / last, and the rest of the unit
+    // is a chunk of its own (its K/V uploaded twice, under the other chunks' kernels).
+    struct Chunk { int64_t u0, cu, g0, ng; };
+    std::vector<Chunk> plan;
+    const int64_t gs = std::max<int64_t>(1, G / 4);
+    const bool split_ends = n_chunks >= 4 && units >= 2 && G >= 2;
+    const int64_t mid0 = split_ends ? 1 : 0, mid1 = split_ends ? units - 1 : units;
+    if (split_ends) {
+        plan.push_back({0, 1, 0, gs});
+        plan.push_back({0, 1, gs, G - gs});
+    }
+    for (int64_t u = mid0; u < mid1; u += per) plan.push_back({u, std::min(per, mid1 - u), 0, G});
+    if (split_ends) {
+        plan.push_back({units - 1, 1, 0, G - gs});
+        plan.push_back({units - 1, 1, G - gs, gs});
+    }
     const size_t in_es = p->qkv_dtype == ODF_DTYPE_F32 ? 4 : 2;
     const size_t out_es = p->o_dtype == ODF_DTYPE_F32 ? 4 : 2;
-    const size_t q_unit = static_cast<size_t>(G * M * D), kv_unit = static_cast<size_t>(N * D);
-    const size_t v_unit = static_cast<size_t>(N * DV), o_unit = static_cast<size_t>(G * M * DV);
+    const size_t kv_unit = static_cast<size_t>(N * D), v_unit = static_cast<size_t>(N * DV);
 
     const uint8_t* dmask = nullptr;
     if (p->block_mask) {
@@ -322,23 +340,23 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
     }
     const size_t ws_bytes = odf::workspace_bytes_for(M, N, p->block_mask != nullptr);
 
-    for (int64_t c = 0; c < n_chunks; ++c) {
-        const int64_t u0 = c * per;
-        const int64_t u1 = std::min(units, u0 + per);
-        if (u0 >= u1) break;
-        const int64_t cu = u1 - u0;
+    for (int64_t c = 0; c < static_cast<int64_t>(plan.size()); ++c) {
+        const int64_t u0 = plan[c].u0, cu = plan[c].cu, g0 = plan[c].g0, ng = plan[c].ng;
+        const int64_t h0 = u0 * G + g0;  // first global (batch, q-head) index of the chunk
+        const int64_t nh = cu * ng;      // its query heads
+        const size_t q_head = static_cast<size_t>(M * D), o_head = static_cast<size_t>(M * DV);
         const int slot = static_cast<int>(c % kHostSets);
         cudaStream_t st = s_in;  // this chunk's copies and conversions
         void *dq, *dk, *dv, *dout, *dlse = nullptr, *dstage = nullptr, *dws = nullptr;
-        if ((e = pool.reserve(slot, 0, cu * q_unit * 2, &dq)) != cudaSuccess ||
+        if ((e = pool.reserve(slot, 0, nh * q_head * 2, &dq)) != cudaSuccess ||
             (e = pool.reserve(slot, 1, cu * kv_unit * 2, &dk)) != cudaSuccess ||
             (e = pool.reserve(slot, 2, cu * v_unit * 2, &dv)) != cudaSuccess ||
-            (e = pool.reserve(slot, 3, cu * o_unit * out_es, &dout)) != cudaSuccess)
+            (e = pool.reserve(slot, 3, nh * o_head * out_es, &dout)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
-        if (p->lse && (e = pool.reserve(slot, 4, cu * G * M * sizeof(float), &dlse)) != cudaSuccess)
+        if (p->lse && (e = pool.reserve(slot, 4, nh * M * sizeof(float), &dlse)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
-        if (in_es == 4 &&
-            (e = pool.reserve(slot, 5, cu * std::max(q_unit, std::max(kv_unit, v_unit)) * 4, &dstage)) != cudaSuccess)
+        if (in_es == 4 && (e = pool.reserve(slot, 5, std::max(nh * q_head, cu * std::max(kv_unit, v_unit)) * 4,
+                                            &dstage)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
         if (ws_bytes && (e = pool.reserve(slot, 6, ws_bytes, &dws)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
@@ -354,14 +372,14 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
             const int64_t* bs = r.bs;
             const int64_t foot = (M - 1) * bs[2] + (N - 1) * bs[3] + 1;
             const bool shared = bs[0] == 0 && bs[1] == 0;
-            const int64_t planes = shared ? 1 : cu * G;
+            const int64_t planes = shared ? 1 : nh;
             bias_plane = shared ? 0 : (foot + 3) / 4 * 4;
             void* db = nullptr;
             if ((e = pool.reserve(slot, 7, static_cast<size_t>(shared ? foot : planes * bias_plane) * sizeof(float),
                                   &db)) != cudaSuccess)
                 return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
             for (int64_t j = 0; j < planes && e == cudaSuccess; ++j) {
-                const int64_t gh = u0 * G + j;  // global (batch, q-head) index of this plane
+                const int64_t gh = h0 + j;  // global (batch, q-head) index of this plane
                 const int64_t b = gh / p->heads_q, h = gh % p->heads_q;
                 e = cudaMemcpyAsync(static_cast<float*>(db) + j * bias_plane, p->bias + b * bs[0] + h * bs[1],
                                     static_cast<size_t>(foot) * sizeof(float), cudaMemcpyHostToDevice, st);
@@ -370,11 +388,11 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
             dbias = static_cast<const float*>(db);
         }
 
-        const char* hq = static_cast<const char*>(p->q) + u0 * q_unit * in_es;
+        const char* hq = static_cast<const char*>(p->q) + h0 * q_head * in_es;
         const char* hk = static_cast<const char*>(p->k) + u0 * kv_unit * in_es;
         const char* hv = static_cast<const char*>(p->v) + u0 * v_unit * in_es;
         struct Part { const char* src; void* dst; size_t elems; } parts[3] = {
-            {hq, dq, cu * q_unit}, {hk, dk, cu * kv_unit}, {hv, dv, cu * v_unit}};
+            {hq, dq, nh * q_head}, {hk, dk, cu * kv_unit}, {hv, dv, cu * v_unit}};
         for (const Part& part : parts) {
             if (in_es == 2) {
                 e = cudaMemcpyAsync(part.dst, part.src, part.elems * 2, cudaMemcpyHostToDevice, st);
@@ -398,7 +416,7 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         sub.qkv_dtype = ODF_DTYPE_BF16;
         sub.batch = 1;
         sub.heads_kv = cu;
-        sub.heads_q = cu * G;
+        sub.heads_q = nh;
         sub.block_mask = dmask;
         sub.workspace = dws;
         sub.workspace_bytes = ws_bytes;
@@ -414,13 +432,13 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         // of heads when heads are re-based, so slopes are indexed by head within the batch).
         std::vector<float> slopes;
         if (p->bias_kind == ODF_BIAS_ALIBI) {
-            slopes.resize(static_cast<size_t>(cu * G));
-            for (int64_t j = 0; j < cu * G; ++j) {
-                const int64_t h = ((u0 * G) + j) % p->heads_q;
+            slopes.resize(static_cast<size_t>(nh));
+            for (int64_t j = 0; j < nh; ++j) {
+                const int64_t h = (h0 + j) % p->heads_q;
                 slopes[j] = p->alibi_slopes ? p->alibi_slopes[h] : generated_slope(h, p->heads_q);
             }
             sub.alibi_slopes = slopes.data();
-            if (cu * G > ODF_MAX_EXPLICIT_SLOPES) return fail(ODF_ERR_UNSUPPORTED, "too many heads per chunk for ALiBi");
+            if (nh > ODF_MAX_EXPLICIT_SLOPES) return fail(ODF_ERR_UNSUPPORTED, "too many heads per chunk for ALiBi");
         }
         Resolved rs;
         rc = validate(&sub, false, &rs);
@@ -436,10 +454,10 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         // copy out after the kernel
         e = cudaStreamWaitEvent(s_out, pool.comp_done[slot], 0);
         if (e == cudaSuccess)
-            e = cudaMemcpyAsync(static_cast<char*>(p->o) + u0 * o_unit * out_es, dout, cu * o_unit * out_es,
+            e = cudaMemcpyAsync(static_cast<char*>(p->o) + h0 * o_head * out_es, dout, nh * o_head * out_es,
                                 cudaMemcpyDeviceToHost, s_out);
         if (e == cudaSuccess && p->lse)
-            e = cudaMemcpyAsync(p->lse + u0 * G * M, dlse, cu * G * M * sizeof(float), cudaMemcpyDeviceToHost, s_out);
+            e = cudaMemcpyAsync(p->lse + h0 * M, dlse, nh * M * sizeof(float), cudaMemcpyDeviceToHost, s_out);
         if (e == cudaSuccess) e = cudaEventRecord(pool.out_done[slot], s_out);
         if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
     }
