@@ -213,11 +213,13 @@ int run_device(const odf_fwd_params* p, const Resolved& r, cudaStream_t stream) 
 // Three stages run on their own streams -- copy in (and fp32 -> bf16), the kernel, copy out --
 // over kHostSets rotating buffer sets, so chunk c's upload, chunk c-1's kernel and chunk c-2's
 // download overlap.  Events order a stage after the previous stage of its chunk and a buffer
-// set's reuse after the last stage that read it.
+// set's reuse after the last stage that read it.  Kernels of consecutive chunks alternate
+// between two compute streams, so the next chunk's CTAs take the SMs that the previous
+// chunk's last items leave idle.
 constexpr int kHostSets = 3;
 struct HostPool {
     int device = -1;
-    cudaStream_t streams[3] = {nullptr, nullptr, nullptr};  // copy in, compute, copy out
+    cudaStream_t streams[4] = {nullptr, nullptr, nullptr, nullptr};  // copy in, compute x2, copy out
     cudaEvent_t in_done[kHostSets] = {}, comp_done[kHostSets] = {}, out_done[kHostSets] = {};
     void* buf[kHostSets][8] = {};
     size_t cap[kHostSets][8] = {};
@@ -288,7 +290,7 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         for (int i = 0; i < kHostSets; ++i)
             if (!evs[i] && e == cudaSuccess) e = cudaEventCreateWithFlags(&evs[i], cudaEventDisableTiming);
     if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
-    cudaStream_t s_in = pool.streams[0], s_comp = pool.streams[1], s_out = pool.streams[2];
+    cudaStream_t s_in = pool.streams[0], s_out = pool.streams[3];
 
     // Work is chunked over (batch, kv-head) units; a unit's Q/O rows (its
     // heads_q/heads_kv query heads) and K/V rows are contiguous.
@@ -346,7 +348,8 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         const int64_t nh = cu * ng;      // its query heads
         const size_t q_head = static_cast<size_t>(M * D), o_head = static_cast<size_t>(M * DV);
         const int slot = static_cast<int>(c % kHostSets);
-        cudaStream_t st = s_in;  // this chunk's copies and conversions
+        cudaStream_t st = s_in;                        // this chunk's copies and conversions
+        cudaStream_t s_comp = pool.streams[1 + (c & 1)];  // its kernel
         void *dq, *dk, *dv, *dout, *dlse = nullptr, *dstage = nullptr, *dws = nullptr;
         if ((e = pool.reserve(slot, 0, nh * q_head * 2, &dq)) != cudaSuccess ||
             (e = pool.reserve(slot, 1, cu * kv_unit * 2, &dk)) != cudaSuccess ||
