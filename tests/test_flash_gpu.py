@@ -492,18 +492,22 @@ def test_host_entry_matches_device_entry(in_dtype):
     check_close(o, lse, o_ref, lse_ref, "host entry")
 
 
-@pytest.mark.parametrize("mod", ["alibi", "head_key_bias"])
-def test_host_entry_split_first_and_last_units(mod):
+@pytest.mark.parametrize("mod,in_dtype", [("alibi", "bf16"), ("head_key_bias", "bf16"), ("alibi", "f32")])
+def test_host_entry_split_first_and_last_units(mod, in_dtype):
     """A problem large enough for four or more host chunks (B 1, 32 q-heads over 8 kv-heads,
     N 8192): the first and last kv-head units are split into query-head sub-chunks, whose
-    per-head ALiBi slopes and bias planes are shifted to their heads; the result equals the
-    device entry bit for bit."""
+    per-head ALiBi slopes and bias planes are shifted to their heads, and fp32 inputs are
+    converted per sub-chunk; the result equals the device entry bit for bit."""
     import odf_b200
 
     B, H, Hk, N, D = 1, 32, 8, 8192, 128
     rng = np.random.default_rng(41)
     q, k, v = (np.ascontiguousarray((rng.standard_normal((B, h, N, D)).astype(np.float32).view(np.uint32) >> 16)
                                     .astype(np.uint16)) for h in (H, Hk, Hk))
+    if in_dtype == "f32":  # the same bf16 values, given as fp32 (converted exactly on the device)
+        hq, hk, hv = ((x.astype(np.uint32) << 16).view(np.float32) for x in (q, k, v))
+    else:
+        hq, hk, hv = q, k, v
     kw, dkw = {}, {}
     if mod == "alibi":
         kw["alibi"] = dkw["alibi"] = True
@@ -511,7 +515,7 @@ def test_host_entry_split_first_and_last_units(mod):
         bias = rng.standard_normal((1, H, 1, N)).astype(np.float32)
         kw["bias"], dkw["bias"] = bias, to_dev(bias, _torch().float32)
     lse = np.empty((B, H, N), dtype=np.float32)
-    o, _ = odf_b200.flash_fwd_host(q, k, v, causal=True, lse_out=lse, **kw)
+    o, _ = odf_b200.flash_fwd_host(hq, hk, hv, causal=True, lse_out=lse, **kw)
     torch = _torch()
     tq, tk, tv = (torch.from_numpy(x.astype(np.int16)).view(torch.bfloat16).cuda() for x in (q, k, v))
     o_dev = torch.empty((B, H, N, D), dtype=torch.float32, device="cuda")
