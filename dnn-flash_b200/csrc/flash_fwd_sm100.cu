@@ -68,8 +68,8 @@ constexpr int kLaunchRegs = 168;
 // mods, or the bias tensor) need 112 registers there, the others keep 200 for the softmax.
 template <int MOD>
 struct RegSplit {
-    static constexpr int kCtrl = (MOD == 3 || MOD >= 4) ? 112 : 104;
-    static constexpr int kSoftmax = (MOD == 3 || MOD >= 4) ? 192 : 200;
+    static constexpr int kCtrl = ((MOD & 7) == 3 || (MOD & 7) >= 4) ? 112 : 104;
+    static constexpr int kSoftmax = ((MOD & 7) == 3 || (MOD & 7) >= 4) ? 192 : 200;
     static_assert(128 * kCtrl + 256 * kSoftmax <= kThreads * kLaunchRegs, "register split exceeds the launch");
     static_assert(kCtrl % 8 == 0 && kSoftmax % 8 == 0 && kSoftmax <= 256, "setmaxnreg operands");
 };
@@ -84,7 +84,9 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleLog2 = 8.0f;
 
 // Score-mod variants: ALiBi and the same-shape bias are exclusive (one BiasKind per call).
-enum ModFlags { kModAlibi = 1, kModSoftcap = 2, kModBias = 4 };
+// kModSkipMax marks the plain-score variant for long KV ranges whose unmasked tiles skip the
+// row-max pass (the low three bits select the score mods).
+enum ModFlags { kModAlibi = 1, kModSoftcap = 2, kModBias = 4, kModSkipMax = 8 };
 
 template <int D>
 struct Config {
@@ -331,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t n_items = static_cast<int64_t>(args.batch) * args.heads_q * args.n_pairs;
     // Greedy item assignment is compiled into the plain d = 128 kernel only (the shapes whose
     // K/V outgrows L2 and whose speed depends on it); the other variants keep the fixed order.
-    constexpr bool kDyn = (MOD == 0 && D == 128);
+    constexpr bool kDyn = ((MOD & 7) == 0 && D == 128);
     volatile int64_t* item_q = reinterpret_cast<volatile int64_t*>(smem + Cfg::kOffQueue);
 
     if (threadIdx.x == 0) {
@@ -719,6 +721,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 float s[128];
                 ptx::tmem_ld128(s_addr, s);
+                if constexpr ((MOD & kModSkipMax) != 0 && !Cfg::kSepP) {
+                    // Unmasked tile, every row with a running max: the exponentials are taken against
+                    // that max straight away and the largest P is checked afterwards.  The max moves
+                    // only past 2^8; then S is read again and the general path below runs, so the
+                    // result is the same as with the max pass first.
+                    const bool interior = k0 + kTileK <= args.n && !(e & bitmap_bit) &&
+                                          !(args.causal && k0 + kTileK - 1 > q0);
+                    if (args.scale_log2 > 0.0f && interior && __all_sync(0xffffffffu, m_run != -INFINITY)) {
+                        const uint64_t mul2 = ptx::f32x2(args.scale_log2);
+                        const uint64_t neg2 = ptx::f32x2(-m_run);
+                        uint64_t sum2[4] = {0, 0, 0, 0};
+                        float mx4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                        for (int c = 0; c < 128; c += 2) {
+                            const uint64_t x = ptx::ffma2(ptx::f32x2(s[c], s[c + 1]), mul2, neg2);
+                            const float p0 = ptx::ex2(ptx::lo_f32(x));
+                            const float p1 = ptx::ex2(ptx::hi_f32(x));
+                            sum2[(c >> 1) & 3] = ptx::fadd2(sum2[(c >> 1) & 3], ptx::f32x2(p0, p1));
+                            mx4[(c >> 1) & 3] = ptx::fmax3(mx4[(c >> 1) & 3], p0, p1);
+                            s[c >> 1] = __uint_as_float(ptx::pack_bf16x2(p0, p1));
+                        }
+                        const float pmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+                        if (!__any_sync(0xffffffffu, pmax > 256.0f)) {
+                            const uint64_t sum4 =
+                                ptx::fadd2(ptx::fadd2(sum2[0], sum2[1]), ptx::fadd2(sum2[2], sum2[3]));
+                            l_run += ptx::lo_f32(sum4) + ptx::hi_f32(sum4);
+                            ptx::tmem_st64_nowait(p_addr, reinterpret_cast<const uint32_t*>(s));
+                            ptx::tmem_st_wait();
+                            ptx::tc_fence_before();
+                            ptx::mbar_arrive(&bars.p_full[qtile]);
+                            phases = (phases ^ 1u) | 4u;
+                            if (row == 0 && args.visits) {
+                                args.visits[(static_cast<int64_t>(rec->bh) * args.n_qt + (q0 / kTileQ)) * args.n_kt +
+                                            kt] = 1;
+                            }
+                            continue;
+                        }
+                        ptx::tmem_ld128(s_addr, s);  // a row's max moved: the general path, from S again
+                    }
+                }
                 if (Cfg::kSepP) {  // S_i is in registers: the next S_i may be computed now
                     ptx::tc_fence_before();
                     ptx::mbar_arrive(&bars.s_free[qtile]);
@@ -730,7 +772,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // score_mod: s*scale (+ ALiBi or bias tensor) (-> soft-cap), in log2 units
                 // (attention.cpp:619).  Without a score_mod the scale is folded into the exponent
                 // below (raw scores).
-                const bool raw = (MOD == 0) && (args.scale_log2 > 0.0f);
+                const bool raw = ((MOD & 7) == 0) && (args.scale_log2 > 0.0f);
                 if (MOD & kModBias) {
                     // same-shape additive bias (qk_score_tile.cpp:28-47): s*scale + bias(qi, kj) in
                     // the units of the next step (natural before a soft-cap, log2 otherwise).
@@ -1163,6 +1205,12 @@ template <int D>
 cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FwdArgs& a,
                      int mod, dim3 grid, cudaStream_t stream) {
     const size_t smem = Config<D>::kSmemBytes;
+    if constexpr (D == 128) {
+        if (mod == kModSkipMax) {
+            flash_fwd_kernel<128, kModSkipMax><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a);
+            return cudaGetLastError();
+        }
+    }
     switch (mod) {
         case 0: flash_fwd_kernel<D, 0><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a); break;
         case 1: flash_fwd_kernel<D, 1><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a); break;
@@ -1234,6 +1282,7 @@ int ensure_device_ready(int device, const char** err) {
     if (e == cudaSuccess) e = set_kernel_attrs<128, 3>(&regs_ok);
     if (e == cudaSuccess) e = set_kernel_attrs<128, 4>(&regs_ok);
     if (e == cudaSuccess) e = set_kernel_attrs<128, 6>(&regs_ok);
+    if (e == cudaSuccess) e = set_kernel_attrs<128, kModSkipMax>(&regs_ok);
     if (e == cudaSuccess && !regs_ok) {
         st.status_code = ODF_ERR_UNSUPPORTED;
         *err = "flash kernel built with an unexpected register count (the warp register split needs 168)";
@@ -1335,7 +1384,10 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
         a.tile_list = list;
         a.tile_count = count;
     }
-    const int mod = (L.has_alibi ? kModAlibi : 0) | (L.has_softcap ? kModSoftcap : 0) | (L.has_bias ? kModBias : 0);
+    int mod = (L.has_alibi ? kModAlibi : 0) | (L.has_softcap ? kModSoftcap : 0) | (L.has_bias ? kModBias : 0);
+    // long KV ranges of a plain score: the variant whose unmasked tiles skip the row-max pass (on
+    // short or block-masked problems, with few unmasked tiles per row, it measured slower)
+    if (mod == 0 && L.head_dim == 128 && a.mode != kModeList && a.n_kt >= 48) mod = kModSkipMax;
     // persistent grid: one CTA per SM (the kernel's shared memory allows one), at most one per item
     const int64_t n_items = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;
     int sm_count = 0;
