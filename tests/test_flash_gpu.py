@@ -492,6 +492,18 @@ def test_host_entry_matches_device_entry(in_dtype):
     check_close(o, lse, o_ref, lse_ref, "host entry")
 
 
+@pytest.mark.parametrize("spike_tile", [1, 30, 47])
+def test_running_max_jump_on_long_key_range(spike_tile):
+    """48 KV tiles (the variant that takes the exponentials against the running max before
+    checking it): one K tile scaled by 8 lifts its scores far above the running max, so rows whose
+    max moves past 2^8 are recomputed with the max pass; O and LSE still match the oracle."""
+    q, k, v = make_qkv(51 + spike_tile, 1, 2, 2, 256, 48 * 128, 128)
+    k[:, :, spike_tile * 128:(spike_tile + 1) * 128, :] *= 8.0  # a power of two: still bf16 values
+    o, lse = run_gpu(q, k, v)
+    o_ref, lse_ref = oracle_fwd(q, k, v)
+    check_close(o, lse, o_ref, lse_ref, f"spike in tile {spike_tile}")
+
+
 @pytest.mark.parametrize("mod,in_dtype", [("alibi", "bf16"), ("head_key_bias", "bf16"), ("alibi", "f32")])
 def test_host_entry_split_first_and_last_units(mod, in_dtype):
     """A problem large enough for four or more host chunks (B 1, 32 q-heads over 8 kv-heads,
