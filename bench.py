@@ -1,11 +1,14 @@
 #!/usr/bin/env python3
 """Benchmark: attention forward TFLOP/s (mask-adjusted) on 1..8 B200s.
 
-Workload (per rank, weak scaling): BASELINE config 5 -- causal GQA forward,
-B=1, Hq=64, Hkv=8, N=32768, d=128, bf16 Q/K/V i.i.d. N(0,1) generated on the
-device from a per-rank seed, bf16 O + fp32 LSE.  One step = one forward over
-the rank's inputs (Q 512 MiB + K/V 128 MiB + O 512 MiB, all larger than L2,
-so no flush is needed between steps).  FLOP are mask-adjusted:
+Workload: BASELINE config 5 -- causal GQA forward, B=1, Hq=64, Hkv=8, N=32768,
+d=128, bf16 Q/K/V i.i.d. N(0,1) generated on the device from a seed, bf16 O +
+fp32 LSE.  By default (strong scaling) its 8 (batch, kv-head) groups are split
+evenly over the ranks: 8/4/2/1 groups per GPU at 1/2/4/8 GPUs, each group with
+its 8 query heads, so no K/V crosses ranks; `--scaling weak` runs the whole
+config on every rank instead.  One step = one forward over the rank's inputs
+(at N=1: Q 512 MiB + K/V 128 MiB + O 512 MiB, all larger than L2, so no flush
+is needed between steps).  FLOP are mask-adjusted:
 4 * d * (#unmasked (q, k) pairs) per head = 4*128*64*N(N+1)/2 = 1.7593e13.
 
 Ranks share nothing on the data path (heads are independent): the only
@@ -216,6 +219,35 @@ def reduce_max(values, dist):
     return [float(v) for v in t.cpu()]
 
 
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def gpu_numa_cpus(local):
+    """(NUMA node, its CPU list) of GPU `local`, from sysfs; (None, None) if unknown."""
+    import torch
+
+    props = torch.cuda.get_device_properties(local)
+    try:
+        bus = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        node = int(Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text().strip())
+        if node < 0:
+            return None, None
+        cpus = set()
+        for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        return node, cpus & os.sched_getaffinity(0) or None
+    except (AttributeError, OSError, ValueError):
+        return None, None
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -275,6 +307,58 @@ def cpu_reference_sample(cfg, rows, steps, warmup, use_ref=True):
     }
 
 
+def shipped_cpu_bench(timeout_s=120):
+    """The reference's own CPU benchmark as shipped (benchmarks/bench_attention.cpp, built unmodified
+    into oracle/_ref/onednn_flash_bench): a fixed M=N=128, d=64 causal shape; its exit code is its
+    own parity verdict (tiled == standard within 1e-5).  Returns its timings in ms."""
+    exe = ROOT / "oracle" / "_ref" / "onednn_flash_bench"
+    if not exe.exists():
+        return {"available": False, "why": "oracle/_ref/onednn_flash_bench not built"}
+    try:
+        r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=timeout_s)
+    except (OSError, subprocess.TimeoutExpired) as exc:
+        return {"available": False, "why": f"{type(exc).__name__}: {exc}"}
+    out = {"available": True, "exit_code": r.returncode, "parity_ok": r.returncode == 0}
+    for line in r.stdout.splitlines():
+        key, _, val = line.partition(":")
+        if key.startswith("shape"):
+            out["shape"] = val.strip()
+        elif key.endswith("_ms"):
+            try:
+                out[key.strip()] = float(val)
+            except ValueError:
+                pass
+    return out
+
+
+def batched_single_thread_sample(cfg, rows):
+    """The reference's flash_attention_batched_qk_pv_tile as shipped (serial over (batch x head), one
+    thread) on a head subset of the workload: one query head per kv-head group of batch 0 (the
+    reference has no GQA, so each sampled head gets its group's K/V), causal prefix [0, rows),
+    tiles 16x32.  ALiBi and soft-cap are left out (the batched entry takes no bias functor)."""
+    import numpy as np
+
+    import oracle
+
+    if not oracle.ref_available():
+        return None
+    Hq, Hkv, D = cfg["Hq"], cfg["Hkv"], cfg["D"]
+    G = Hq // Hkv
+    rng = np.random.default_rng(8)
+    R = rows
+    q = oracle.round_bf16(rng.standard_normal((1, Hkv, R, D)).astype(np.float32) * cfg["in_scale"])
+    k = oracle.round_bf16(rng.standard_normal((1, Hkv, R, D)).astype(np.float32) * cfg["in_scale"])
+    v = oracle.round_bf16(rng.standard_normal((1, Hkv, R, D)).astype(np.float32) * cfg["in_scale"])
+    sub = dict(cfg, N=R, mask=None)
+    flop = flop_per_unit_pairs(sub) * Hkv
+    t0 = time.perf_counter()
+    oracle.ref_fwd("batched", q, k, v, causal=cfg["causal"], q_block=16, k_block=32)
+    dt = time.perf_counter() - t0
+    return {"value": flop / dt / 1e12, "unit": "TFLOP/s", "cores": 1, "seconds": dt,
+            "sample": f"{Hkv} q-heads (head g*{G} of each kv group, batch 0), causal prefix [0,{R}), "
+                      f"{flop / 1e9:.2f} GFLOP, tiles 16x32, score mods off"}
+
+
 def run_reference_arm(args, cfg, workload):
     world, rank, _ = dist_setup()
     if rank != 0:
@@ -291,11 +375,15 @@ def run_reference_arm(args, cfg, workload):
         "warmup": args.warmup,
         "ms_per_step": base["seconds_per_step"] * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": workload, "sample_rows": rows, "note": "CPU reference on host cores"},
+        "config": {"workload": workload, "sample_rows": rows, "same_config": False,
+                   "sample": f"every (batch, q-head) unit of the workload on its causal prefix [0,{rows}): "
+                             "an exact sub-problem (causal rows < R see only keys < R), timed at its own "
+                             "size; value = its mask-adjusted FLOP / time, not extrapolated to N",
+                   "note": f"CPU reference on host cores ({cpu_model()})"},
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -381,8 +469,14 @@ def run_ours(args, cfg, workload):
     if status != 0:
         raise RuntimeError(f"device status {status}: an in-kernel wait timed out")
 
-    # e2e through the host entry (pinned host buffers, H2D + D2H inside the timed region)
+    # e2e through the host entry (pinned host buffers, H2D + D2H inside the timed region).  The
+    # rank's thread runs on its GPU's NUMA node while it fills the pinned buffers (first touch
+    # places the pages there) and while it drives the copies.
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    numa_node, numa_cpus = gpu_numa_cpus(local)
+    saved_affinity = os.sched_getaffinity(0)
+    if numa_cpus:
+        os.sched_setaffinity(0, numa_cpus)
     hq = q.cpu().pin_memory()
     hk = k.cpu().pin_memory()
     hv = v.cpu().pin_memory()
@@ -403,6 +497,7 @@ def run_ours(args, cfg, workload):
     for _ in range(e2e_steps):
         e2e_step()
     e2e_s = (time.perf_counter() - t0) / e2e_steps
+    os.sched_setaffinity(0, saved_affinity)
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
     d2h = ho.numel() * ho.element_size() + hl.numel() * 4
 
@@ -454,7 +549,8 @@ def run_ours(args, cfg, workload):
             },
             "roofline": roof,
             "e2e": {"value": world * flop_rank / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world, "path": "odf_flash_fwd_host (pinned host buffers)"},
+                    "d2h_bytes_per_step": d2h * world, "path": "odf_flash_fwd_host (pinned host buffers)",
+                    "host_numa": ({"node": numa_node, "cpus": len(numa_cpus)} if numa_cpus else "not bound")},
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(),
         }
@@ -465,6 +561,13 @@ def run_ours(args, cfg, workload):
             except Exception as exc:  # the CPU checker is optional for the GPU number
                 result["cpu_baseline"] = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "unavailable",
                                           "sample": f"{type(exc).__name__}: {exc}"}
+            result["cpu_baseline"]["cpu_model"] = cpu_model()
+            result["cpu_baseline"]["host_cores"] = os.cpu_count()
+            try:
+                result["cpu_baseline"]["batched_single_thread"] = batched_single_thread_sample(cfg, args.cpu_rows // 3)
+            except Exception as exc:
+                result["cpu_baseline"]["batched_single_thread"] = {"unavailable": f"{type(exc).__name__}: {exc}"}
+            result["cpu_baseline"]["shipped_bench"] = shipped_cpu_bench()
         print(json.dumps(result), flush=True)
     if dist:
         dist.barrier()
@@ -483,8 +586,9 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=3072, help="prefix rows of the CPU baseline sample")
     ap.add_argument("--ref-rows", type=int, default=1536, help="prefix rows per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
-                    help="weak: the config per GPU (default); strong: the config split over the GPUs")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong",
+                    help="strong (default): the config's (batch, kv-head) groups split over the GPUs; "
+                         "weak: the whole config on every GPU")
     ap.add_argument("--seq-len", type=int, default=None,
                     help="override N (profiling of a smaller case only; the BASELINE config is the default)")
     args = ap.parse_args()

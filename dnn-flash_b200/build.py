@@ -18,8 +18,11 @@ CSRC = PACKAGE_DIR / "csrc"
 LIB = PACKAGE_DIR / "lib" / "libodf_sm100.so"
 SOURCES = [CSRC / "flash_fwd_sm100.cu", CSRC / "odf_capi.cu"]
 CXX_API_SOURCES = [CSRC / "onednn_flash_api.cpp", CSRC / "planner.cpp"]
-DEPS = SOURCES + CXX_API_SOURCES + [CSRC / "sm100_ptx.cuh", CSRC / "odf_internal.h"] + sorted(
+DEPS = SOURCES + CXX_API_SOURCES + [CSRC / "sm100_ptx.cuh", CSRC / "softmax_math.cuh", CSRC / "odf_internal.h"] + sorted(
     (ROOT / "include").rglob("*.h*"))
+# Test-only device wrappers of the softmax arithmetic helpers (error-bound tests).
+MATH_CHECK_SRC = ROOT / "tests" / "cuda" / "math_check.cu"
+MATH_CHECK_LIB = ROOT / "tests" / "cuda" / "lib" / "libodf_math_check.so"
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -54,6 +57,22 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+def build_math_check(force: bool = False, verbose: bool = False) -> Path:
+    """tests/cuda/lib/libodf_math_check.so (test infrastructure, not part of the library)."""
+    deps = [MATH_CHECK_SRC, CSRC / "softmax_math.cuh", CSRC / "sm100_ptx.cuh"]
+    if not force and MATH_CHECK_LIB.exists() and all(
+            p.stat().st_mtime <= MATH_CHECK_LIB.stat().st_mtime for p in deps):
+        return MATH_CHECK_LIB
+    MATH_CHECK_LIB.parent.mkdir(parents=True, exist_ok=True)
+    cmd = [nvcc(), *NVCC_FLAGS, f"-I{CSRC}", "-shared", "-o", str(MATH_CHECK_LIB) + ".tmp", str(MATH_CHECK_SRC)]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    os.replace(str(MATH_CHECK_LIB) + ".tmp", MATH_CHECK_LIB)
+    return MATH_CHECK_LIB
+
+
 if __name__ == "__main__":
     build_library(force="--force" in sys.argv, verbose=True)
+    build_math_check(force="--force" in sys.argv, verbose=True)
     print(LIB)

@@ -38,9 +38,9 @@
 // The softmax raises its running max only when a tile's max exceeds it by more than
 // 2^8; the O rescale this needs is done by the softmax thread itself (PV_i(j-1) has
 // completed once S_i(j) has, since a tcgen05 commit tracks all earlier MMAs).
-// Every wait is bounded (2 s); on timeout the CTA records ODF_ERR_DEVICE_TIMEOUT
-// in the device status word, all roles leave their loops, in-flight copies and
-// MMAs are drained, and the TMEM columns are freed before the CTA exits.
+// Every wait is bounded (args.wait_limit_ns, 2 s unless a test lowers it); on timeout the
+// CTA records ODF_ERR_DEVICE_TIMEOUT in the device status word, all roles leave their loops,
+// in-flight copies and MMAs are drained, and the TMEM columns are freed before the CTA exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -51,6 +51,7 @@
 
 #include "odf_internal.h"
 #include "sm100_ptx.cuh"
+#include "softmax_math.cuh"
 
 namespace odf {
 
@@ -75,7 +76,6 @@ struct RegSplit {
 };
 constexpr uint32_t kTmemCols = 512;
 constexpr int kItemQueue = 4;  // entries of the shared-memory queue of work items
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kChunkBytes = 128 * 128;  // 128 rows x 128 bytes (64 bf16)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -256,48 +256,12 @@ __device__ __forceinline__ uint4 row_allow_bits(const FwdArgs& a, int qi, int k0
     return allow;
 }
 
-// 2^x for a pair on the FMA pipe.  At d = 64 the MUFU unit (16 ex2 per clock per SM) is the
-// binding limit, so part of the columns take this path instead.  x is clamped to -127, split as
-// x = j + f with j = rint(x) (by adding and subtracting 1.5 * 2^23) and f in [-0.5, 0.5]; 2^f
-// comes from a degree-3 polynomial whose coefficients were fitted here for minimax relative
-// error with p(0) = 1 (max relative error 1.0e-4), and j is added to the exponent field.
-// x = -127 (so also -inf) gives exactly +0; other x below -126 give values in [0, 2^-126).
-constexpr float kExp2C1 = 0.6932829022407532f;
-constexpr float kExp2C2 = 0.2422109693288803f;
-constexpr float kExp2C3 = 0.055009059607982635f;
-
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
-    const uint64_t xc = ptx::f32x2(fmaxf(ptx::lo_f32(x), -127.0f), fmaxf(ptx::hi_f32(x), -127.0f));
-    const uint64_t t = ptx::fadd2(xc, ptx::f32x2(12582912.0f));   // 1.5 * 2^23 + rint(x)
-    const uint64_t j = ptx::fadd2(t, ptx::f32x2(-12582912.0f));   // rint(x), exact
-    const uint64_t f = ptx::ffma2(j, ptx::f32x2(-1.0f), xc);      // x - rint(x), exact
-    uint64_t p = ptx::ffma2(ptx::f32x2(kExp2C3), f, ptx::f32x2(kExp2C2));
-    p = ptx::ffma2(p, f, ptx::f32x2(kExp2C1));
-    p = ptx::ffma2(p, f, ptx::f32x2(1.0f));
-    // the low bits of t hold 1.5 * 2^23 + j; shifted left by 23 only j << 23 remains (mod 2^32)
-    const uint32_t lo = static_cast<uint32_t>(p) + (static_cast<uint32_t>(t) << 23);
-    const uint32_t hi = static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
-    return (static_cast<uint64_t>(hi) << 32) | lo;
-}
-
 // Column pairs (index c/2 mod 8) whose exponentials use exp2_poly2, per head dim.
 #ifndef ODF_POLY_MASK_D64
 #define ODF_POLY_MASK_D64 0x80  // one pair in eight: the best of 0, 1/8, 1/4, 3/8, 1/2 measured at d = 64
 #endif
 template <int D>
 __host__ __device__ constexpr uint32_t poly_exp2_mask() { return D == 64 ? ODF_POLY_MASK_D64 : 0u; }
-
-// softcap * tanh(t) * log2(e) for a pair of scores given u = 2 log2(e) t (t = score / softcap),
-// from tanh|t| = 2 / (1 + e) - 1 with e = 2^(-|u|) in (0, 1]: two MUFU operations per score (ex2
-// and the reciprocal, both within a few ulps), no overflow for any |t|, the scale folded into one
-// FMA and the sign restored from u.  Absolute error a few fp32 ulps of softcap * log2(e).
-__device__ __forceinline__ uint64_t softcap2(uint64_t u, uint64_t cap2x, uint64_t neg_cap) {
-    const float e0 = ptx::ex2(-fabsf(ptx::lo_f32(u)));
-    const float e1 = ptx::ex2(-fabsf(ptx::hi_f32(u)));
-    const uint64_t den = ptx::fadd2(ptx::f32x2(e0, e1), ptx::f32x2(1.0f));
-    const uint64_t r = ptx::f32x2(ptx::rcp(ptx::lo_f32(den)), ptx::rcp(ptx::hi_f32(den)));
-    return ptx::ffma2(r, cap2x, neg_cap) ^ (u & 0x8000000080000000ull);
-}
 
 template <int D, int MOD>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -390,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int qs = it % kItemQueue;
                         if (it >= kItemQueue &&
                             !(ok = ptx::mbar_wait(&bars.item_empty[qs], ((it / kItemQueue) - 1) & 1, abort_flag,
-                                                  args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)))
+                                                  args.status, ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns)))
                             break;
                         item_q[qs] = k;
                         ptx::mbar_arrive(&bars.item_full[qs]);
@@ -402,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (I.n_entries == 0) continue;
                     // Q of this item replaces the previous item's once its last S MMAs have read it.
                     if (q_loads > 0 && !(ok = ptx::mbar_wait(bars.q_empty, (q_loads - 1) & 1, abort_flag, args.status,
-                                                             ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)))
+                                                             ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns)))
                         break;
                     ptx::mbar_arrive_expect_tx(bars.q_full, (I.valid1 ? 2 : 1) * Cfg::kTileBytes);
                     for (int c = 0; c < Cfg::kChunks; ++c) {
@@ -422,28 +386,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const int s = t % kSlots;
                             const int use = t / kSlots;
                             if (use >= 1 && !(ok = ptx::mbar_wait(&bars.slot_empty[s], (use - 1) & 1, abort_flag,
-                                                                  args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)))
+                                                                  args.status, ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns)))
                                 break;
                             uint8_t* dst = sSlots + s * Cfg::kTileBytes;
-                            ptx::mbar_arrive_expect_tx(&bars.slot_full[s], Cfg::kTileBytes);
-                            const void* map = half == 0 ? static_cast<const void*>(&tmK) : static_cast<const void*>(&tmV);
-                            for (int c = 0; c < Cfg::kChunks; ++c) {
-                                ptx::tma_load_4d(dst + c * kChunkBytes, map, &bars.slot_full[s], c * 64, kt * kTileK,
-                                                 I.hk, I.b);
+                            if (!(t == args.stall_load && blockIdx.x == 0)) {  // test-only injected stall
+                                ptx::mbar_arrive_expect_tx(&bars.slot_full[s], Cfg::kTileBytes);
+                                const void* map =
+                                    half == 0 ? static_cast<const void*>(&tmK) : static_cast<const void*>(&tmV);
+                                for (int c = 0; c < Cfg::kChunks; ++c) {
+                                    ptx::tma_load_4d(dst + c * kChunkBytes, map, &bars.slot_full[s], c * 64,
+                                                     kt * kTileK, I.hk, I.b);
+                                }
                             }
                             ++issued;
                         }
                     }
                 }
-                if (!ok || *abort_flag) {
-                    // Let copies already issued land before the CTA's shared memory is released.
+                {
+                    // Let copies already issued land before the CTA's shared memory is released (on
+                    // the normal path the MMA warp has waited for them already; after an abort some
+                    // were never consumed).  Older loads landed before their slot was reused.
                     volatile int no_abort = 0;
                     const int first = issued > kSlots ? issued - kSlots : 0;
                     for (int t = first; t < issued; ++t) {
+                        if (t == args.stall_load && blockIdx.x == 0) continue;  // never issued
                         ptx::mbar_wait(&bars.slot_full[t % kSlots], (t / kSlots) & 1, &no_abort, nullptr, 0,
-                                       kWaitLimitNs);
+                                       args.wait_limit_ns);
                     }
-                    if (q_loads > 0) ptx::mbar_wait(bars.q_full, (q_loads - 1) & 1, &no_abort, nullptr, 0, kWaitLimitNs);
+                    if (q_loads > 0) ptx::mbar_wait(bars.q_full, (q_loads - 1) & 1, &no_abort, nullptr, 0, args.wait_limit_ns);
                 }
             }
         } else if (warp == kWarpMma) {
@@ -468,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 auto issue_s = [&](int i, int slot) -> bool {
                     if (Cfg::kSepP && s_count[i] > 0) {
                         if (!ptx::mbar_wait(&bars.s_free[i], (s_count[i] - 1) & 1, abort_flag, args.status,
-                                            ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
+                                            ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns))
                             return false;
                         ptx::tc_fence_after();
                     }
@@ -486,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // O_i += P_i V (TS: P_i from TMEM, V MN-major from shared memory; M=128, N=D, K=128).
                 auto issue_pv = [&](int i, int slot) -> bool {
                     if (!ptx::mbar_wait(&bars.p_full[i], pv_count[i] & 1, abort_flag, args.status,
-                                        ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs))
+                                        ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns))
                         return false;
                     ptx::tc_fence_after();
                     const uint32_t vd = v_lo0 + static_cast<uint32_t>(slot) * kSlotStep;
@@ -505,12 +475,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 };
                 auto wait_full = [&](int t) -> bool {
                     return ptx::mbar_wait(&bars.slot_full[t % kSlots], (t / kSlots) & 1, abort_flag, args.status,
-                                          ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+                                          ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns);
                 };
                 // Q of the next item, then S_0/S_1 of its first KV tile (ring index tk).
                 auto start_item = [&](const Item& In, uint32_t en, int tk) -> bool {
                     if (!ptx::mbar_wait(bars.q_full, q_loads & 1, abort_flag, args.status, ODF_ERR_DEVICE_TIMEOUT,
-                                        kWaitLimitNs))
+                                        args.wait_limit_ns))
                         return false;
                     ++q_loads;
                     if (!wait_full(tk)) return false;
@@ -531,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (kDyn && args.sched) {
                             const int qs = it % kItemQueue;
                             if (!ptx::mbar_wait(&bars.item_full[qs], (it / kItemQueue) & 1, abort_flag, args.status,
-                                                ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)) {
+                                                ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns)) {
                                 ok = false;
                                 return false;
                             }
@@ -603,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // Drain the MMAs already issued before the TMEM columns are freed.
                     volatile int no_abort = 0;
                     ptx::tc_commit(bars.drain);
-                    ptx::mbar_wait(bars.drain, 0, &no_abort, nullptr, 0, kWaitLimitNs);
+                    ptx::mbar_wait(bars.drain, 0, &no_abort, nullptr, 0, args.wait_limit_ns);
                 }
             }
         }
@@ -642,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) {  // one reader per warp takes the item from the queue
                     const int qs = it % kItemQueue;
                     if (ptx::mbar_wait(&bars.item_full[qs], (it / kItemQueue) & 1, abort_flag, args.status,
-                                       ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs)) {
+                                       ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns)) {
                         item = item_q[qs];
                         ptx::mbar_arrive(&bars.item_empty[qs]);
                     } else {
@@ -707,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // Waits are per thread; the warp re-converges (and agrees) before the
                 // .sync.aligned TMEM accesses that follow.
                 const bool got = ptx::mbar_wait(&bars.s_full[qtile], phases & 1u, abort_flag, args.status,
-                                                ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+                                                ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
@@ -943,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // and before O_i is rescaled (S_i(j) can complete ahead of it there).
                 if (Cfg::kSepP && (phases & 16u)) {
                     const bool done = ptx::mbar_wait(&bars.pv_done[qtile], (phases >> 3) & 1u, abort_flag,
-                                                     args.status, ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+                                                     args.status, ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns);
                     phases ^= 8u;
                     if (!__all_sync(0xffffffffu, done)) {
                         ok = false;
@@ -981,7 +951,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool fed = (phases & 4u) != 0;
             if (fed) {
                 ok = ptx::mbar_wait(&bars.o_done[qtile], (phases >> 1) & 1u, abort_flag, args.status,
-                                    ODF_ERR_DEVICE_TIMEOUT, kWaitLimitNs);
+                                    ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns);
                 phases ^= 2u;
                 ptx::tc_fence_after();
             }
@@ -1160,10 +1130,15 @@ __device__ int g_device_status;
 
 // ------------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
 std::once_flag g_encode_once;
 
+// Per device: set up once per CUDA context.  Kernel attributes and the status word's address
+// belong to the context the module was loaded into, so a new context on the device (after
+// cudaDeviceReset, or a context the caller made current) repeats the set-up.
 struct DeviceState {
     bool ready = false;
+    void* ctx = nullptr;
     int status_code = ODF_OK;
     int* status_ptr = nullptr;
     int sm_count = 0;
@@ -1234,14 +1209,26 @@ size_t workspace_bytes_for(int64_t seqlen_q, int64_t seqlen_k, bool has_mask) {
     return kSchedBytes + ((list + 255) & ~static_cast<size_t>(255)) + ((count + 255) & ~static_cast<size_t>(255));
 }
 
-int ensure_device_ready(int device, const char** err) {
-    if (device < 0 || device >= kMaxDevices) {
-        *err = "device index out of range";
-        return ODF_ERR_NO_DEVICE;
-    }
-    std::lock_guard<std::mutex> lock(g_device_mutex);
-    DeviceState& st = g_devices[device];
-    if (st.ready) return ODF_OK;
+void* current_context() {
+    static CtxGetCurrentFn fn_ptr = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn_ptr = reinterpret_cast<CtxGetCurrentFn>(fn);
+        }
+    });
+    CUcontext ctx = nullptr;
+    if (fn_ptr == nullptr || fn_ptr(&ctx) != CUDA_SUCCESS) return nullptr;
+    return ctx;
+}
+
+namespace {
+
+int setup_device_locked(int device, DeviceState& st, const char** err) {
+    st.ready = false;
     if (st.status_code != ODF_OK) {
         *err = "device previously failed initialisation (needs an sm_100 GPU)";
         return st.status_code;
@@ -1296,8 +1283,23 @@ int ensure_device_ready(int device, const char** err) {
     }
     st.status_ptr = static_cast<int*>(sp);
     st.sm_count = prop.multiProcessorCount;
+    st.ctx = current_context();  // the runtime calls above made the device's context current
     st.ready = true;
     return ODF_OK;
+}
+
+}  // namespace
+
+int ensure_device_ready(int device, const char** err) {
+    if (device < 0 || device >= kMaxDevices) {
+        *err = "device index out of range";
+        return ODF_ERR_NO_DEVICE;
+    }
+    void* ctx = current_context();
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    DeviceState& st = g_devices[device];
+    if (st.ready && ctx != nullptr && st.ctx == ctx) return ODF_OK;
+    return setup_device_locked(device, st, err);
 }
 
 int* device_status_ptr(int device) {
@@ -1338,6 +1340,7 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
     if (rc != ODF_OK) return rc;
     a.status = device_status_ptr(device);
     a.n_pairs = (a.n_qt + 1) / 2;
+    if (a.wait_limit_ns == 0) a.wait_limit_ns = kDefaultWaitLimitNs;
 
     CUtensorMap tq, tk, tv;
     if (encode_bf16_4d(&tq, L.q, L.head_dim, a.m, a.heads_q, a.batch, L.q_strides) != CUDA_SUCCESS ||

@@ -18,6 +18,10 @@
 namespace {
 
 thread_local std::string t_last_error;
+// Test hooks (odf_debug_set_wait): limit of the in-kernel waits and an injected stall, applied
+// to the launches this thread makes.
+thread_local uint64_t t_wait_limit_ns = 0;  // 0 = the default (2 s)
+thread_local int32_t t_stall_load = -1;      // -1 = off
 
 int fail(int code, const std::string& msg) {
     t_last_error = msg;
@@ -171,6 +175,8 @@ odf::FwdLaunch make_launch(const odf_fwd_params* p, const Resolved& r) {
     a.mask_qblocks = static_cast<int32_t>(std::min<int64_t>(p->mask_qblocks, 0x7fffffff));
     a.mask_kblocks = static_cast<int32_t>(std::min<int64_t>(p->mask_kblocks, 0x7fffffff));
     a.visits = p->tile_visits;
+    a.wait_limit_ns = t_wait_limit_ns;
+    a.stall_load = t_stall_load;
     if (p->bias_kind == ODF_BIAS_SAME_SHAPE) {
         a.bias = p->bias;
         a.bias_s0 = r.bs[0];
@@ -518,6 +524,15 @@ int odf_device_status(int32_t* status_out, int32_t clear) {
 
 const char* odf_last_error(void) { return t_last_error.c_str(); }
 
+int odf_debug_set_wait(uint64_t limit_ns, int32_t stall_load) {
+    if (limit_ns != 0 && (limit_ns < 1000000ull || limit_ns > 60000000000ull))
+        return fail(ODF_ERR_INVALID_ARG, "wait limit must be 0 (default) or within [1 ms, 60 s]");
+    if (stall_load < -1) return fail(ODF_ERR_INVALID_ARG, "stall_load must be -1 (off) or a load index >= 0");
+    t_wait_limit_ns = limit_ns;
+    t_stall_load = stall_load;
+    return ODF_OK;
+}
+
 const char* odf_version(void) { return "dnn-flash-b200 0.1.0 (sm_100a tcgen05/TMA forward)"; }
 
 }  // extern "C"
@@ -532,26 +547,33 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[ODF_NOALLOC_SCRATCH_B
 namespace {
 
 struct NoAllocDevice {
-    bool ready = false;
+    void* ctx = nullptr;      // the CUDA context the address below belongs to
     void* scratch = nullptr;
 };
 NoAllocDevice g_noalloc[64];
 std::mutex g_noalloc_mutex;
 
-// Resolves the device address of g_noalloc_scratch for the current device (first call only).
+// Device address of g_noalloc_scratch in the current device's current context.  A __device__
+// array's address belongs to the context the module was loaded into, so it is looked up again
+// whenever that context changes (cudaDeviceReset, a context the caller made current).
 int noalloc_scratch_for_current_device(void** out) {
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) return fail(ODF_ERR_NO_DEVICE, "no CUDA device");
     if (device < 0 || device >= 64) return fail(ODF_ERR_NO_DEVICE, "device index out of range");
+    // the same capability and set-up checks, and status codes, as odf_flash_fwd_sm100
+    const char* err = "";
+    const int rc = odf::ensure_device_ready(device, &err);
+    if (rc != ODF_OK) return fail(rc, err);
+    void* ctx = odf::current_context();
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
     NoAllocDevice& d = g_noalloc[device];
-    if (!d.ready) {
+    if (d.scratch == nullptr || ctx == nullptr || d.ctx != ctx) {
         void* ptr = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
         if (e != cudaSuccess || ptr == nullptr)
             return fail(ODF_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch) failed: ") + cudaGetErrorString(e));
         d.scratch = ptr;
-        d.ready = true;
+        d.ctx = odf::current_context();
     }
     *out = d.scratch;
     return ODF_OK;

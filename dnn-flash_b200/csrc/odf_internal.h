@@ -57,7 +57,16 @@ struct FwdArgs {
     // every unit).
     unsigned long long* sched;
     int32_t units_per_block;
+    // Limit of every bounded in-kernel wait (ns); the host fills in the default of 2 s unless a
+    // caller lowered it through odf_debug_set_wait.
+    uint64_t wait_limit_ns;
+    // Failure injection for tests (-1 = off): the producer warp of CTA 0 leaves out its ring load
+    // number stall_load (neither the bytes nor the copy), so the MMA warp's wait for that slot runs
+    // out and the abort path runs: status word set, roles leave, copies and MMAs drained.
+    int32_t stall_load;
 };
+
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;
 
 // The first kSchedBytes of a workspace hold the item counter; block-mask tile lists follow.
 constexpr size_t kSchedBytes = 256;
@@ -88,8 +97,13 @@ int launch_tile_map(int32_t m, int32_t n, int32_t causal, const uint8_t* mask, i
 // fp32 -> bf16 conversion kernel.
 int launch_convert_f32_bf16(const float* in, uint16_t* out, int64_t count, cudaStream_t stream);
 
-// Per-device one-time setup (capability check, kernel attributes, status word).
+// Per-device setup (capability check, kernel attributes, status word), redone when the device's
+// current CUDA context changes (after cudaDeviceReset, or another context made current).
 int ensure_device_ready(int device, const char** err);
+
+// The calling thread's current CUDA context (driver handle, NULL if none), fetched through the
+// runtime's driver entry point so the library needs no -lcuda.
+void* current_context();
 
 // Device address of the status word bounded waits write to (current device).
 int* device_status_ptr(int device);

@@ -124,11 +124,14 @@ size_t odf_fwd_workspace_size(const odf_fwd_params* p);
  * tile lists.  Limit: the lists take about ceil(seqlen_q/256) *
  * ceil(seqlen_k/128) * 4 bytes; larger problems are rejected with
  * ODF_ERR_UNSUPPORTED.  The first call on a device looks up the array's device
- * address (a one-time, non-allocating runtime call); make that first call
- * before any stream capture.  All calls share the one array; each launch clears
- * the counter and rewrites the lists it reads, so nothing else needs to start at
- * zero, but calls that overlap on the GPU, on different streams, race on it:
- * serialise them.
+ * address (a one-time, non-allocating runtime call, repeated only if the
+ * device's CUDA context changes); make that first call before any stream
+ * capture.  All calls share the one array, which keeps what the last call left
+ * there.  A launch that hands out work through the counter (long plain d = 128
+ * problems) clears it first, and a block-mask launch rewrites the lists before
+ * reading them; the other launches read nothing from the array.  So nothing
+ * needs to start at zero, but calls that overlap on the GPU, on different
+ * streams, race on the array: serialise them.
  * No counterpart in the reference (its workspace is always caller-owned).
  */
 int odf_flash_fwd_sm100_noalloc(const odf_fwd_params* p, void* stream);
@@ -162,6 +165,20 @@ int odf_convert_f32_to_bf16(const float* in, uint16_t* out, int64_t count, void*
 /* Reads (and, if `clear`, resets) the device-side status word of the current
    device that bounded in-kernel waits set on timeout.  Synchronises the device. */
 int odf_device_status(int32_t* status_out, int32_t clear);
+
+/*
+ * Test hook for the bounded in-kernel waits (no counterpart in the reference).
+ * Applies to the forward launches this host thread makes from now on:
+ *   limit_ns    limit of every in-kernel wait; 0 restores the default (2 s),
+ *               otherwise within [1 ms, 60 s];
+ *   stall_load  -1 = off; n >= 0 makes CTA 0 leave out its n-th K/V tile load,
+ *               so a wait for it runs out: the kernel then records
+ *               ODF_ERR_DEVICE_TIMEOUT in the status word (odf_device_status),
+ *               drains its copies and MMAs, frees its tensor memory and returns,
+ *               and the context stays usable.  That launch's output is undefined.
+ * Failure drills and tests use it; a production caller never needs it.
+ */
+int odf_debug_set_wait(uint64_t limit_ns, int32_t stall_load);
 
 /* Message for the last non-zero status returned on this host thread. */
 const char* odf_last_error(void);

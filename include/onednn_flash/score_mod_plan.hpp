@@ -88,9 +88,12 @@ ScoreModPlan make_score_mod_plan(ScoreModKind requested_kind,
                                  bool one_dnn_post_ops_available);
 
 // GPU (sm_100a) plan of the register epilogue: accepts F32 and BF16, scale,
-// BiasKind::None / AlibiGenerated, and an optional soft-cap; every other bias
-// layout reports FallbackReason::UnsupportedBiasLayout.  Signatures extend the
-// reference's format with ":softcap" when a soft-cap is requested.
+// BiasKind::None / AlibiGenerated / SameShapeTile (a strided fp32 bias tensor,
+// whose zero strides also express row and column broadcasts), and an optional
+// soft-cap.  BroadcastRow / BroadcastCol report FallbackReason::UnsupportedBroadcast
+// (pass them as a SameShapeTile tensor with zero strides), every other bias layout
+// FallbackReason::UnsupportedBiasLayout.  Signatures extend the reference's format
+// with ":softcap" when a soft-cap is requested.
 ScoreModPlan make_sm100_score_mod_plan(ScoreModKind requested_kind,
                                        DataType dtype,
                                        bool has_scale,

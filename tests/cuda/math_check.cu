@@ -1,0 +1,61 @@
+// math_check.cu -- test-only device wrappers around the softmax warps' arithmetic helpers
+// (dnn-flash_b200/csrc/softmax_math.cuh), so their error bounds can be checked on the GPU
+// against exact values computed on the host.  Built into tests/cuda/lib/libodf_math_check.so
+// by dnn-flash_b200/build.py; not part of the library.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "softmax_math.cuh"
+
+namespace {
+
+// y_poly[i] = exp2_poly2(x[i]) and y_mufu[i] = ex2.approx(x[i]), pairs (2i, 2i+1) per thread.
+__global__ void exp2_kernel(const float* __restrict__ x, float* __restrict__ y_poly, float* __restrict__ y_mufu,
+                            int64_t n_pairs) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n_pairs) return;
+    const float x0 = x[2 * i], x1 = x[2 * i + 1];
+    const uint64_t p = odf::exp2_poly2(odf::ptx::f32x2(x0, x1));
+    y_poly[2 * i] = odf::ptx::lo_f32(p);
+    y_poly[2 * i + 1] = odf::ptx::hi_f32(p);
+    y_mufu[2 * i] = odf::ptx::ex2(x0);
+    y_mufu[2 * i + 1] = odf::ptx::ex2(x1);
+}
+
+// y[i] = softcap * tanh(s[i] / softcap) in natural units, through the kernel's softcap2 (which
+// returns the value times log2 e), pairs (2i, 2i+1) per thread.
+__global__ void softcap_kernel(const float* __restrict__ s, float* __restrict__ y, int64_t n_pairs, float softcap) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n_pairs) return;
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float k = 2.0f * kLog2e / softcap;
+    const uint64_t u = odf::ptx::f32x2(s[2 * i] * k, s[2 * i + 1] * k);
+    const uint64_t r = odf::softcap2(u, odf::ptx::f32x2(2.0f * softcap * kLog2e), odf::ptx::f32x2(-softcap * kLog2e));
+    y[2 * i] = odf::ptx::lo_f32(r) / kLog2e;
+    y[2 * i + 1] = odf::ptx::hi_f32(r) / kLog2e;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Device pointers, n even; synchronous.  Returns a cudaError_t value (0 = success).
+int odf_math_check_exp2(const float* x, float* y_poly, float* y_mufu, int64_t n) {
+    if (n <= 0 || (n & 1)) return static_cast<int>(cudaErrorInvalidValue);
+    const int64_t pairs = n / 2;
+    exp2_kernel<<<static_cast<unsigned>((pairs + 255) / 256), 256>>>(x, y_poly, y_mufu, pairs);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return static_cast<int>(e);
+}
+
+int odf_math_check_softcap(const float* s, float* y, int64_t n, float softcap) {
+    if (n <= 0 || (n & 1) || !(softcap > 0.0f)) return static_cast<int>(cudaErrorInvalidValue);
+    const int64_t pairs = n / 2;
+    softcap_kernel<<<static_cast<unsigned>((pairs + 255) / 256), 256>>>(s, y, pairs, softcap);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return static_cast<int>(e);
+}
+
+}  // extern "C"

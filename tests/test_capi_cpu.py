@@ -110,3 +110,16 @@ def test_null_params_and_status_pointer():
 def test_declared_symbols_parser_sees_all_headers():
     assert odf_b200.HEADER_PATHS, "include/*.h missing"
     assert all(n.startswith("odf_") for n in odf_b200.declared_symbols())
+
+
+def test_debug_wait_hook_validation():
+    """odf_debug_set_wait takes 0 (default) or a limit within [1 ms, 60 s], and -1 (off) or a
+    load index; it only sets this thread's launch options (no CUDA call)."""
+    lib = odf_b200.load_library()
+    lib.odf_debug_set_wait.argtypes = [C.c_uint64, C.c_int32]
+    assert lib.odf_debug_set_wait(500_000, -1) == odf_b200.ODF_ERR_INVALID_ARG
+    assert "limit" in odf_b200.last_error()
+    assert lib.odf_debug_set_wait(61_000_000_000, -1) == odf_b200.ODF_ERR_INVALID_ARG
+    assert lib.odf_debug_set_wait(20_000_000, -2) == odf_b200.ODF_ERR_INVALID_ARG
+    assert lib.odf_debug_set_wait(20_000_000, 3) == odf_b200.ODF_OK
+    assert lib.odf_debug_set_wait(0, -1) == odf_b200.ODF_OK

@@ -84,11 +84,12 @@ def test_config2_causal_d64():
 
 
 def test_config3_alibi_softcap_reduced():
-    """c3 at reduced length: causal + ALiBi 2^(-8h/H) + soft-cap 50, inputs N(0,1)*0.5, bf16 O."""
+    """c3 at reduced length with the config's 32 heads (so the slopes are c3's 2^(-8h/32)):
+    causal + ALiBi + soft-cap 50, inputs N(0,1)*0.5, bf16 O."""
     torch = _torch()
     import oracle
 
-    H = 8
+    H = 32
     q, k, v = make_qkv(3, 1, H, H, 1024, 1024, 128, scale=0.5)
     o, lse = run_gpu(q, k, v, causal=True, alibi=True, softcap=50.0, out_dtype=torch.bfloat16)
     o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, alibi_slopes=oracle.alibi_slopes(H), softcap=50.0)
@@ -332,6 +333,51 @@ def test_config3_full_size_rows():
         got = o[b, h, rows].float().cpu().numpy()
         assert np.abs(got - o_ref).max() <= O_MAX_ABS
         assert np.abs(lse[b, h, rows].cpu().numpy() - lse_ref).max() <= LSE_MAX_ABS
+
+
+def test_config3_full_size_prefix_vs_oracle():
+    """c3 at full size (B2 H32 N8192 d128, ALiBi 2^(-8h/32) + soft-cap 50, inputs N(0,1)*0.5,
+    bf16 O): causal rows < R see only keys < R, so the prefix [0, R) of four (batch, head) units
+    is an exact sub-problem, checked against the oracle with those heads' slopes."""
+    torch = _torch()
+    import odf_b200
+    import oracle
+
+    B, H, N, D = 2, 32, 8192, 128
+    g = torch.Generator(device="cuda").manual_seed(34)
+    q, k, v = ((torch.randn((B, H, N, D), generator=g, device="cuda") * 0.5).to(torch.bfloat16) for _ in range(3))
+    o, lse = odf_b200.flash_fwd(q, k, v, causal=True, alibi=True, softcap=50.0, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.isfinite(o.float()).all() and torch.isfinite(lse).all()
+    R = 768
+    units = [(0, 0), (1, 31), (0, 17), (1, 6)]
+    slopes = oracle.alibi_slopes(H)
+    sel = lambda t: np.stack([t[b, h, :R].float().cpu().numpy() for b, h in units])[None]
+    o_ref, lse_ref = oracle_fwd(sel(q), sel(k), sel(v), causal=True,
+                                alibi_slopes=np.float32([slopes[h] for _, h in units]), softcap=50.0)
+    check_close(sel(o), np.stack([lse[b, h, :R].cpu().numpy() for b, h in units])[None], o_ref, lse_ref,
+                "c3 full-size prefix")
+
+
+def test_config4_full_size_units_vs_oracle():
+    """c4 at full size (B8 H16 N4096 d128, 128x128 window-4 + prefix-4 block mask with causal,
+    22.3% of the blocks): every row of three (batch, head) units against the oracle."""
+    torch = _torch()
+    import odf_b200
+    import oracle
+
+    B, H, N, D = 8, 16, 4096, 128
+    mask = oracle.sliding_window_prefix_mask(N // 128)
+    g = torch.Generator(device="cuda").manual_seed(44)
+    q, k, v = (torch.randn((B, H, N, D), generator=g, device="cuda").to(torch.bfloat16) for _ in range(3))
+    o, lse = odf_b200.flash_fwd(q, k, v, causal=True, block_mask=mask, mask_block=(128, 128),
+                                out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    units = [(0, 0), (3, 7), (7, 15)]
+    sel = lambda t: np.stack([t[b, h].float().cpu().numpy() for b, h in units])[None]
+    o_ref, lse_ref = oracle_fwd(sel(q), sel(k), sel(v), causal=True, mask=mask, mask_block=(128, 128))
+    check_close(sel(o), np.stack([lse[b, h].cpu().numpy() for b, h in units])[None], o_ref, lse_ref,
+                "c4 full size")
 
 
 def test_config5_full_size_prefix_and_tail():

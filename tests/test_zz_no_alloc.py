@@ -1,12 +1,14 @@
 """odf_flash_fwd_sm100_noalloc: the entry point for callers that cannot allocate
 device memory (fixed-budget serving loops, plugins whose host owns the allocator,
-foreign-language bindings without an allocator).  It keeps its block-mask tile lists
-in a library-owned static device array instead of a caller workspace.
+foreign-language bindings without an allocator).  It keeps its work-item counter and
+block-mask tile lists in a library-owned static device array instead of a caller
+workspace.
 
 Checked through the C ABI against odf_flash_fwd_sm100 (which uses a caller
-workspace) on the same inputs, on two calls in a row so that a second call over
-the scratch left by the first is covered too.  This file is collected last so a
-failure here never hides the rest of the suite.
+workspace) on the same inputs, and on the greedy-counter path also against the
+oracle, on two calls in a row so that a second call over the scratch left by the
+first is covered too.  This file is collected last so a failure here never hides
+the rest of the suite.
 """
 from __future__ import annotations
 
@@ -33,7 +35,10 @@ def _lib():
     return lib
 
 
-def _run(entry, q, k, v, mask, mask_block, causal, use_workspace):
+def _run(entry, q, k, v, mask, mask_block, causal, use_workspace, want_counter=False):
+    """One call of `entry` on NaN-filled O/LSE (rows a call leaves out stay NaN).  With
+    want_counter, also returns the work-item counter the workspace entry left in its workspace
+    (0 when the launch used the fixed order, which never touches it)."""
     import odf_b200
     import torch
 
@@ -48,12 +53,15 @@ def _run(entry, q, k, v, mask, mask_block, causal, use_workspace):
     if use_workspace:
         nbytes = _lib().odf_fwd_workspace_size(C.byref(p))
         if nbytes:
-            ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
             p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
     rc = entry(C.byref(p), C.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0, odf_b200.last_error()
     torch.cuda.synchronize()
+    counter = int(ws[:8].cpu().numpy().view(np.uint64)[0]) if (want_counter and ws is not None) else None
     del keep, ws
+    if want_counter:
+        return o.cpu().numpy(), lse.cpu().numpy(), counter
     return o.cpu().numpy(), lse.cpu().numpy()
 
 
@@ -89,6 +97,37 @@ def test_noalloc_matches_workspace_entry_two_calls(case):
         _compare(o, lse, o_ref, lse_ref)
         results.append(o)
     assert not np.array_equal(results[0], results[1])  # the two calls really ran on different inputs
+
+
+def test_noalloc_greedy_counter_path_two_calls_vs_oracle():
+    """A problem long enough for the greedy, L2-blocked item order (plain score, d=128, K/V of
+    16 (batch, kv-head) units = 64 MB, over the 32 MB block size), which hands out work through a
+    counter: with the no-allocation entry that counter lives in the library's static scratch.
+    Two calls in a row on NaN-filled outputs: a counter left uncleared by the first call would
+    leave rows of the second unwritten.  Each call equals the workspace entry bit for bit (the
+    item order does not change any item's arithmetic) and its causal prefix rows match the
+    oracle.  N = 8192 (64 KV tiles) also selects the variant that skips the row-max pass."""
+    import torch
+
+    import oracle
+
+    lib = _lib()
+    B, H, N, D = 1, 16, 8192, 128
+    n_items = B * H * (N // 256)  # work items: pairs of 128-row query tiles per (batch, head)
+    for call in range(2):
+        g = torch.Generator(device="cuda").manual_seed(70 + call)
+        q, k, v = (torch.randn((B, H, N, D), generator=g, device="cuda").to(torch.bfloat16) for _ in range(3))
+        o_ws, lse_ws, counter = _run(lib.odf_flash_fwd_sm100, q, k, v, None, (128, 128), True,
+                                     use_workspace=True, want_counter=True)
+        # the workspace entry chose the counter: every item taken, plus one failed take per CTA
+        assert counter is not None and counter > n_items, f"counter {counter}: greedy order not used"
+        o, lse = _run(lib.odf_flash_fwd_sm100_noalloc, q, k, v, None, (128, 128), True, use_workspace=False)
+        assert np.isfinite(o).all() and np.isfinite(lse).all(), f"call {call}: rows left unwritten"
+        assert np.array_equal(o, o_ws) and np.array_equal(lse, lse_ws), f"call {call}: differs from workspace entry"
+        R, heads = 512, [0, 7, 15]
+        qs, ks, vs = (t[:, heads, :R].float().cpu().numpy() for t in (q, k, v))
+        o_ref, lse_ref = oracle.flash_fwd(qs, ks, vs, causal=True)
+        _compare(o[:, heads, :R], lse[:, heads, :R], o_ref, lse_ref)
 
 
 def test_noalloc_rejects_lists_beyond_scratch():
