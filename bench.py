@@ -230,7 +230,8 @@ def cpu_model():
 
 
 def gpu_numa_cpus(local):
-    """(NUMA node, its CPU list) of GPU `local`, from sysfs; (None, None) if unknown."""
+    """(NUMA node, its CPUs usable here) of GPU `local`, from sysfs; (reason, None) when the
+    platform gives no node for the GPU."""
     import torch
 
     props = torch.cuda.get_device_properties(local)
@@ -238,14 +239,15 @@ def gpu_numa_cpus(local):
         bus = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
         node = int(Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text().strip())
         if node < 0:
-            return None, None
+            return f"sysfs reports no NUMA node for {bus}", None
         cpus = set()
         for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
             lo, _, hi = part.partition("-")
             cpus.update(range(int(lo), int(hi or lo) + 1))
-        return node, cpus & os.sched_getaffinity(0) or None
-    except (AttributeError, OSError, ValueError):
-        return None, None
+        cpus &= os.sched_getaffinity(0)
+        return (node, cpus) if cpus else (f"no CPU of node {node} is usable here", None)
+    except (AttributeError, OSError, ValueError) as exc:
+        return f"{type(exc).__name__}: {exc}", None
 
 
 def dist_setup():
@@ -450,11 +452,16 @@ def run_ours(args, cfg, workload):
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    # With per-step events (small configs) the GPU would otherwise sit idle while the host enqueues
+    # the launch after the start event, and that host time would be counted: a short spin kernel
+    # (torch's, ~50 us) after the flush keeps the GPU busy until the launch is queued.
+    spin_cycles = 100_000 if flush is not None else 0
     with ClockSampler(local) as clocks:
         t_begin.record(stream)
         for i in range(args.steps):
             if flush is not None:
                 flush.zero_()
+                torch.cuda._sleep(spin_cycles)
             starts[i].record(stream)
             step()
             ends[i].record(stream)
@@ -520,7 +527,8 @@ def run_ours(args, cfg, workload):
                 "peak_kind": f"{peak_kind} HBM copy bandwidth", "tflops": achieved}
     roof.update({"traffic": profiled_traffic(args.config, args.seq_len), "algorithmic_bytes": alg_bytes,
                  "kernel": f"flash_fwd_kernel<{D},{mod}>", "avg_launch_ms": avg_launch_ms})
-    l2_note = ("L2 flushed (256 MB write) between timed steps; value from per-step events" if flush is not None
+    l2_note = ("L2 flushed (256 MB write) between timed steps, then a ~50 us spin kernel so the launch is "
+               "queued before its start event; value from per-step events" if flush is not None
                else f"inputs and outputs ({alg_bytes / 2 ** 20:.0f} MiB) larger than twice L2; no flush needed")
     result = None
     if rank == 0:
@@ -550,7 +558,8 @@ def run_ours(args, cfg, workload):
             "roofline": roof,
             "e2e": {"value": world * flop_rank / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "path": "odf_flash_fwd_host (pinned host buffers)",
-                    "host_numa": ({"node": numa_node, "cpus": len(numa_cpus)} if numa_cpus else "not bound")},
+                    "host_numa": ({"node": numa_node, "cpus": len(numa_cpus)} if numa_cpus
+                                  else f"not bound ({numa_node})")},
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(),
         }
