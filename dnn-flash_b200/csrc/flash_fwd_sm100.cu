@@ -741,8 +741,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
                 // score_mod: s*scale (+ ALiBi or bias tensor) (-> soft-cap), in log2 units
                 // (attention.cpp:619).  Without a score_mod the scale is folded into the exponent
-                // below (raw scores).
+                // below (raw scores); with a soft-cap, s[] holds tanh(t) and softcap * log2(e) is.
                 const bool raw = ((MOD & 7) == 0) && (args.scale_log2 > 0.0f);
+                const float fold = (MOD & kModSoftcap) ? args.softcap * kLog2e : (raw ? args.scale_log2 : 1.0f);
                 if (MOD & kModBias) {
                     // same-shape additive bias (qk_score_tile.cpp:28-47): s*scale + bias(qi, kj) in
                     // the units of the next step (natural before a soft-cap, log2 otherwise).
@@ -809,14 +810,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (MOD & kModSoftcap) {
+                    // t = (s * scale + ALiBi) / softcap, with 1/softcap folded into the FMAs that form
+                    // it; s[] keeps tanh(t) and the exponent below multiplies by softcap * log2(e)
                     const float base = static_cast<float>(k0 - qi);
-                    // u = (s * scale + ALiBi) * 2 log2(e) / softcap, the soft-cap's argument
-                    const float kSoftcapU = 2.0f * kLog2e * args.inv_softcap;
-                    const uint64_t scale2 = ptx::f32x2(args.scale * kSoftcapU);
-                    const uint64_t slope2 = ptx::f32x2(slope * kSoftcapU);
-                    const uint64_t sb2 = ptx::f32x2(slope * base * kSoftcapU);
-                    const uint64_t cap2x = ptx::f32x2(2.0f * args.softcap * kLog2e);
-                    const uint64_t neg_cap = ptx::f32x2(-args.softcap * kLog2e);
+                    const uint64_t scale2 = ptx::f32x2(args.scale * args.inv_softcap);
+                    const uint64_t slope2 = ptx::f32x2(slope * args.inv_softcap);
+                    const uint64_t sb2 = ptx::f32x2(slope * base * args.inv_softcap);
 #pragma unroll
                     for (int c = 0; c < 128; c += 2) {
                         uint64_t x = ptx::f32x2(s[c], s[c + 1]);
@@ -825,11 +824,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                              slope2, sb2);
                             x = ptx::ffma2(x, scale2, bias);
                         } else if (MOD & kModBias) {  // the bias pass left s * scale + bias
-                            x = ptx::fmul2(x, ptx::f32x2(kSoftcapU));
+                            x = ptx::fmul2(x, ptx::f32x2(args.inv_softcap));
                         } else {
                             x = ptx::fmul2(x, scale2);
                         }
-                        const uint64_t y = softcap2(x, cap2x, neg_cap);
+                        const uint64_t y = tanh2(x);
                         s[c] = ptx::lo_f32(y);
                         s[c + 1] = ptx::hi_f32(y);
                     }
@@ -875,7 +874,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 8; c < 128; c += 2) mx8[(c >> 1) & 7] = ptx::fmax3(mx8[(c >> 1) & 7], s[c], s[c + 1]);
                 float tile_max = ptx::fmax3(ptx::fmax3(mx8[0], mx8[1], mx8[2]), ptx::fmax3(mx8[3], mx8[4], mx8[5]),
                                             fmaxf(mx8[6], mx8[7]));
-                if (raw) tile_max *= args.scale_log2;
+                if (raw || (MOD & kModSoftcap)) tile_max *= fold;
                 float alpha = 1.0f;
                 if (m_run == -INFINITY) {
                     m_run = tile_max;  // first valid tile of this row: O holds zeros so far
@@ -888,7 +887,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // (element c/2 is written only after s[c] and s[c+1] were consumed).
                 uint64_t sum2[4] = {0, 0, 0, 0};
                 {
-                    const uint64_t mul2 = ptx::f32x2(raw ? args.scale_log2 : 1.0f);
+                    const uint64_t mul2 = ptx::f32x2(fold);
                     const uint64_t neg2 = ptx::f32x2(-m_use);
 #pragma unroll
                     for (int c = 0; c < 128; c += 2) {

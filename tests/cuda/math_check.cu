@@ -22,17 +22,15 @@ __global__ void exp2_kernel(const float* __restrict__ x, float* __restrict__ y_p
     y_mufu[2 * i + 1] = odf::ptx::ex2(x1);
 }
 
-// y[i] = softcap * tanh(s[i] / softcap) in natural units, through the kernel's softcap2 (which
-// returns the value times log2 e), pairs (2i, 2i+1) per thread.
+// y[i] = softcap * tanh(s[i] / softcap) as the kernel forms it: t = s / softcap, tanh2(t), times
+// softcap (the kernel folds softcap * log2 e into its exponent instead), pairs (2i, 2i+1).
 __global__ void softcap_kernel(const float* __restrict__ s, float* __restrict__ y, int64_t n_pairs, float softcap) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n_pairs) return;
-    constexpr float kLog2e = 1.4426950408889634f;
-    const float k = 2.0f * kLog2e / softcap;
-    const uint64_t u = odf::ptx::f32x2(s[2 * i] * k, s[2 * i + 1] * k);
-    const uint64_t r = odf::softcap2(u, odf::ptx::f32x2(2.0f * softcap * kLog2e), odf::ptx::f32x2(-softcap * kLog2e));
-    y[2 * i] = odf::ptx::lo_f32(r) / kLog2e;
-    y[2 * i + 1] = odf::ptx::hi_f32(r) / kLog2e;
+    const float inv = 1.0f / softcap;
+    const uint64_t th = odf::tanh2(odf::ptx::f32x2(s[2 * i] * inv, s[2 * i + 1] * inv));
+    y[2 * i] = odf::ptx::lo_f32(th) * softcap;
+    y[2 * i + 1] = odf::ptx::hi_f32(th) * softcap;
 }
 
 }  // namespace

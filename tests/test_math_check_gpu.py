@@ -6,8 +6,11 @@ values computed on the host in float64.
   in eight at d = 64.  Bound: relative error <= 1.02e-4 wherever 2^x is a normal float
   (x >= -126); exactly +0 at x <= -127 and at -inf; below 2^-126 in between.  The hardware
   ex2.approx on the same inputs is reported beside it for scale.
-* softcap2: softcap * tanh(s / softcap) from 2 / (1 + 2^(-|u|)) - 1 with the MUFU ex2 and
-  reciprocal.  Bound: absolute error <= 2e-6 * softcap over |s| up to 40 * softcap.
+* tanh2: the soft-cap softcap * tanh(s / softcap) from the MUFU tanh.approx.f32.  PTX documents
+  only a 2^-11 relative bound for that instruction; on sm_100 it measures 7.8e-6 absolute at
+  worst, and the attention parity tolerances (LSE 1e-3 with soft-caps down to 5) rely on that,
+  so this test pins an absolute error <= 1e-5 * softcap over |s| up to 40 * softcap: a GPU or
+  driver whose tanh.approx is less accurate fails here, before the parity tests.
 
 The device side is tests/cuda/math_check.cu, a test-only library around the same header the
 kernel includes.
@@ -24,7 +27,7 @@ pytestmark = pytest.mark.gpu
 
 LIB = Path(__file__).resolve().parent / "cuda" / "lib" / "libodf_math_check.so"
 EXP2_REL_BOUND = 1.02e-4
-SOFTCAP_ABS_BOUND = 2e-6  # times softcap
+SOFTCAP_ABS_BOUND = 1e-5  # times softcap
 
 
 def _lib():
