@@ -453,9 +453,9 @@ def run_ours(args, cfg, workload):
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     # With per-step events (small configs) the GPU would otherwise sit idle while the host enqueues
-    # the launch after the start event, and that host time would be counted: a short spin kernel
-    # (torch's, ~50 us) after the flush keeps the GPU busy until the launch is queued.
-    spin_cycles = 100_000 if flush is not None else 0
+    # the launch after the start event, and that host time would be counted: a spin kernel
+    # (torch's, ~1 ms) after the flush keeps the GPU busy until the launch is queued.
+    spin_cycles = 2_000_000 if flush is not None else 0
     with ClockSampler(local) as clocks:
         t_begin.record(stream)
         for i in range(args.steps):
@@ -527,7 +527,7 @@ def run_ours(args, cfg, workload):
                 "peak_kind": f"{peak_kind} HBM copy bandwidth", "tflops": achieved}
     roof.update({"traffic": profiled_traffic(args.config, args.seq_len), "algorithmic_bytes": alg_bytes,
                  "kernel": f"flash_fwd_kernel<{D},{mod}>", "avg_launch_ms": avg_launch_ms})
-    l2_note = ("L2 flushed (256 MB write) between timed steps, then a ~50 us spin kernel so the launch is "
+    l2_note = ("L2 flushed (256 MB write) between timed steps, then a ~1 ms spin kernel so the launch is "
                "queued before its start event; value from per-step events" if flush is not None
                else f"inputs and outputs ({alg_bytes / 2 ** 20:.0f} MiB) larger than twice L2; no flush needed")
     result = None
