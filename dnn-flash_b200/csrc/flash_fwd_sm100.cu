@@ -256,12 +256,19 @@ __device__ __forceinline__ uint4 row_allow_bits(const FwdArgs& a, int qi, int k0
     return allow;
 }
 
-// Column pairs (index c/2 mod 8) whose exponentials use exp2_poly2, per head dim.
+// Column pairs (index c/2 mod 8) whose exponentials use exp2_poly2, per head dim and score mod:
+// where the MUFU unit is the binding limit (d = 64, and the soft-capped variants, which spend a
+// second MUFU operation per score on tanh).
 #ifndef ODF_POLY_MASK_D64
 #define ODF_POLY_MASK_D64 0x80  // one pair in eight: the best of 0, 1/8, 1/4, 3/8, 1/2 measured at d = 64
 #endif
-template <int D>
-__host__ __device__ constexpr uint32_t poly_exp2_mask() { return D == 64 ? ODF_POLY_MASK_D64 : 0u; }
+#ifndef ODF_POLY_MASK_SOFTCAP
+#define ODF_POLY_MASK_SOFTCAP 0x80  // one pair in eight: best of 0, 1/8, 1/4, 3/8, 1/2 on c3 and soft-cap-only 8K
+#endif
+template <int D, int MOD>
+__host__ __device__ constexpr uint32_t poly_exp2_mask() {
+    return D == 64 ? ODF_POLY_MASK_D64 : ((MOD & kModSoftcap) ? ODF_POLY_MASK_SOFTCAP : 0u);
+}
 
 template <int D, int MOD>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -893,7 +900,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int c = 0; c < 128; c += 2) {
                         const uint64_t x = ptx::ffma2(ptx::f32x2(s[c], s[c + 1]), mul2, neg2);
                         float p0, p1;
-                        if ((poly_exp2_mask<D>() >> ((c >> 1) & 7)) & 1u) {
+                        if ((poly_exp2_mask<D, MOD>() >> ((c >> 1) & 7)) & 1u) {
                             const uint64_t p = exp2_poly2(x);
                             p0 = ptx::lo_f32(p);
                             p1 = ptx::hi_f32(p);
