@@ -128,29 +128,55 @@ def profiled_traffic(config, seq_len=None):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons of one GPU, sampled every 20 ms with timestamps.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    nvidia-smi takes a moment to start, and a timed region can be shorter than that (c5 on 8 GPUs:
+    about 40 ms), so the sampler starts before the warm-up and the summary keeps the samples whose
+    timestamps fall inside the timed region (mark_start .. mark_end, host wall clock).  The GPU is
+    addressed by UUID, so a rank's local device maps to the right physical GPU."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 20
 
-    def __init__(self, gpu_index):
-        self.gpu_index = gpu_index
+    def __init__(self, local):
+        import torch
+
+        self.target = str(local)
+        try:
+            uuid = str(torch.cuda.get_device_properties(local).uuid)
+            if uuid:
+                self.target = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except (AttributeError, RuntimeError):
+            pass
         self.proc = None
+        self.lines = []
+        self.t0 = self.t1 = None
 
-    def __enter__(self):
+    def start(self):
+        import atexit
+
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms",
+                 str(self.INTERVAL_MS), "-i", self.target], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+            atexit.register(self.stop)  # never leave the sampling loop behind, whatever happens next
+            time.sleep(0.3)  # let it start sampling before the work it is to watch
         except OSError:
             self.proc = None
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    def stop(self):
         if self.proc is not None:
-            time.sleep(0.25)
+            time.sleep(0.05)
             self.proc.terminate()
             try:
                 out, _ = self.proc.communicate(timeout=5)
@@ -158,25 +184,39 @@ class ClockSampler:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
-        return False
+            self.proc = None
 
     def summary(self):
-        sm, smax, reasons = [], None, set()
+        import datetime
+
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        rows = []
+        for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]),
+                             {n for n, v in zip(names, parts[6:10]) if v.lower().startswith("active")}))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        inside = rows
+        note = None
+        if self.t0 is not None and self.t1 is not None:
+            lo, hi = self.t0 - 0.5 * self.INTERVAL_MS / 1e3, self.t1 + 0.5 * self.INTERVAL_MS / 1e3
+            inside = [r for r in rows if lo <= r[0] <= hi]
+            if not inside and rows:  # nothing landed inside: the samples around the region
+                near = sorted(rows, key=lambda r: min(abs(r[0] - self.t0), abs(r[0] - self.t1)))[:2]
+                inside, note = near, "no sample inside the timed region; the two nearest"
+        out = {"sm_mhz": statistics.median(r[1] for r in inside) if inside else None,
+               "sm_max_mhz": inside[0][2] if inside else None,
+               "reasons": sorted(set().union(*[r[3] for r in inside])) if inside else [],
+               "samples": len(inside), "interval_ms": self.INTERVAL_MS,
+               "timed_region_s": (self.t1 - self.t0) if self.t0 is not None and self.t1 is not None else None}
+        if note:
+            out["note"] = note
+        return out
 
 
 def shard_config(cfg, rank, world, scaling):
@@ -441,6 +481,7 @@ def run_ours(args, cfg, workload):
     l2_bytes = 126 * 2 ** 20
     flush = torch.empty(64 * 2 ** 20, dtype=torch.float32, device=dev) if alg_bytes < 2 * l2_bytes else None
 
+    clocks = ClockSampler(local).start()
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
@@ -456,17 +497,19 @@ def run_ours(args, cfg, workload):
     # the launch after the start event, and that host time would be counted: a spin kernel
     # (torch's, ~1 ms) after the flush keeps the GPU busy until the launch is queued.
     spin_cycles = 2_000_000 if flush is not None else 0
-    with ClockSampler(local) as clocks:
-        t_begin.record(stream)
-        for i in range(args.steps):
-            if flush is not None:
-                flush.zero_()
-                torch.cuda._sleep(spin_cycles)
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
-        t_end.record(stream)
-        torch.cuda.synchronize(dev)
+    clocks.mark_start()
+    t_begin.record(stream)
+    for i in range(args.steps):
+        if flush is not None:
+            flush.zero_()
+            torch.cuda._sleep(spin_cycles)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks.mark_end()
+    clocks.stop()
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
