@@ -75,3 +75,32 @@ def test_strong_shards_keep_whole_gqa_groups(world):
 def test_strong_sharding_rejects_uneven_split():
     with pytest.raises(ValueError):
         bench.shard_config(bench.CONFIGS["c1"], 0, 3, "strong")
+
+
+def test_clock_summary_keeps_samples_inside_the_timed_region():
+    """The bench line's `clocks` field: nvidia-smi samples (timestamped, every 20 ms) are kept only
+    when they fall inside the timed region; with none inside, the two nearest are reported and
+    labelled as such.  No GPU and no nvidia-smi needed: the sampler's output is given as text."""
+    import datetime
+
+    s = bench.ClockSampler.__new__(bench.ClockSampler)
+    s.proc = None
+    t = datetime.datetime(2026, 12, 2, 6, 0, 0)
+
+    def line(dt_ms, mhz, power_cap):
+        ts = (t + datetime.timedelta(milliseconds=dt_ms)).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+        cap = "Active" if power_cap else "Not Active"
+        return f"{ts}, 0, {mhz}, 1965, 900.0, 0x0, Not Active, Not Active, Not Active, {cap}"
+
+    s.lines = [line(0, 1965, False), line(100, 1700, True), line(120, 1680, True), line(140, 1690, True),
+               line(400, 1965, False)]
+    s.t0 = (t + datetime.timedelta(milliseconds=95)).timestamp()
+    s.t1 = (t + datetime.timedelta(milliseconds=150)).timestamp()
+    out = s.summary()
+    assert out["samples"] == 3 and out["sm_mhz"] == 1690.0 and out["sm_max_mhz"] == 1965.0
+    assert out["reasons"] == ["sw_power_cap"] and "note" not in out
+    # a region between two samples: the nearest ones, labelled
+    s.t0 = (t + datetime.timedelta(milliseconds=200)).timestamp()
+    s.t1 = (t + datetime.timedelta(milliseconds=230)).timestamp()
+    out = s.summary()
+    assert out["samples"] == 2 and "note" in out
