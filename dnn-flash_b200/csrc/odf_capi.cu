@@ -231,17 +231,37 @@ struct HostPool {
     size_t cap[kHostSets][8] = {};
     void* mask = nullptr;
     size_t mask_cap = 0;
+    // K and V of units split into query-head pieces (problems with fewer than four units):
+    // uploaded once by the unit's first piece, read by all its pieces' kernels.
+    static constexpr int kSplitUnits = 3;
+    void* kvd[kSplitUnits][2] = {};
+    size_t kvd_cap[kSplitUnits][2] = {};
     ~HostPool() {
         // Process teardown may run after the CUDA context is gone; freeing is best-effort.
         for (auto& set : buf)
             for (void*& b : set)
                 if (b) cudaFree(b);
         if (mask) cudaFree(mask);
+        for (auto& pair : kvd)
+            for (void*& b : pair)
+                if (b) cudaFree(b);
         for (auto* evs : {in_done, comp_done, out_done})
             for (int i = 0; i < kHostSets; ++i)
                 if (evs[i]) cudaEventDestroy(evs[i]);
         for (auto& s : streams)
             if (s) cudaStreamDestroy(s);
+    }
+    cudaError_t reserve_kv(int which, int idx, size_t bytes, void** out) {
+        if (kvd_cap[which][idx] < bytes) {
+            if (kvd[which][idx]) cudaFree(kvd[which][idx]);
+            kvd[which][idx] = nullptr;
+            kvd_cap[which][idx] = 0;
+            cudaError_t e = cudaMalloc(&kvd[which][idx], bytes);
+            if (e != cudaSuccess) return e;
+            kvd_cap[which][idx] = bytes;
+        }
+        *out = kvd[which][idx];
+        return cudaSuccess;
     }
     cudaError_t reserve(int slot, int idx, size_t bytes, void** out) {
         if (cap[slot][idx] < bytes) {
@@ -312,19 +332,33 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
     // alone, so with a pipeline of four or more chunks the first and the last unit are split:
     // a quarter of their query heads (at least one) goes first / last, and the rest of the unit
     // is a chunk of its own (its K/V uploaded twice, under the other chunks' kernels).
-    struct Chunk { int64_t u0, cu, g0, ng; };
+    // With fewer than four units (one GPU's share of a GQA problem split over several GPUs, or a
+    // single kv-head) whole units would make a pipeline of one to three chunks, so every unit is
+    // cut into pieces of query heads (about eight pieces in all); a unit's pieces share one upload
+    // of its K/V into a buffer of its own (kvbuf = the unit, kv_up on its first piece).
+    struct Chunk { int64_t u0, cu, g0, ng; int kvbuf; bool kv_up; };
     std::vector<Chunk> plan;
     const int64_t gs = std::max<int64_t>(1, G / 4);
-    const bool split_ends = n_chunks >= 4 && units >= 2 && G >= 2;
-    const int64_t mid0 = split_ends ? 1 : 0, mid1 = split_ends ? units - 1 : units;
-    if (split_ends) {
-        plan.push_back({0, 1, 0, gs});
-        plan.push_back({0, 1, gs, G - gs});
-    }
-    for (int64_t u = mid0; u < mid1; u += per) plan.push_back({u, std::min(per, mid1 - u), 0, G});
-    if (split_ends) {
-        plan.push_back({units - 1, 1, 0, G - gs});
-        plan.push_back({units - 1, 1, G - gs, gs});
+    // Query heads per piece: about eight pieces in all, but each with at least 148 query tiles
+    // (a piece's kernel should fill the GPU), otherwise the units stay whole.
+    int64_t ps = (G + std::min<int64_t>(G, (8 + units - 1) / units) - 1) / std::min<int64_t>(G, (8 + units - 1) / units);
+    while (ps < G && ps * n_qt < 148) ps = std::min(G, 2 * ps);
+    const bool pieces = units < 4 && ps < G && units <= HostPool::kSplitUnits;
+    const bool split_ends = !pieces && n_chunks >= 4 && units >= 2 && G >= 2;
+    if (pieces) {
+        for (int64_t u = 0; u < units; ++u)
+            for (int64_t g = 0; g < G; g += ps) plan.push_back({u, 1, g, std::min(ps, G - g), static_cast<int>(u), g == 0});
+    } else {
+        const int64_t mid0 = split_ends ? 1 : 0, mid1 = split_ends ? units - 1 : units;
+        if (split_ends) {
+            plan.push_back({0, 1, 0, gs, -1, true});
+            plan.push_back({0, 1, gs, G - gs, -1, true});
+        }
+        for (int64_t u = mid0; u < mid1; u += per) plan.push_back({u, std::min(per, mid1 - u), 0, G, -1, true});
+        if (split_ends) {
+            plan.push_back({units - 1, 1, 0, G - gs, -1, true});
+            plan.push_back({units - 1, 1, G - gs, gs, -1, true});
+        }
     }
     const size_t in_es = p->qkv_dtype == ODF_DTYPE_F32 ? 4 : 2;
     const size_t out_es = p->o_dtype == ODF_DTYPE_F32 ? 4 : 2;
@@ -356,10 +390,17 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         const int slot = static_cast<int>(c % kHostSets);
         cudaStream_t st = s_in;                        // this chunk's copies and conversions
         cudaStream_t s_comp = pool.streams[1 + (c & 1)];  // its kernel
+        const int kvbuf = plan[c].kvbuf;
+        const bool kv_up = plan[c].kv_up;
         void *dq, *dk, *dv, *dout, *dlse = nullptr, *dstage = nullptr, *dws = nullptr;
-        if ((e = pool.reserve(slot, 0, nh * q_head * 2, &dq)) != cudaSuccess ||
-            (e = pool.reserve(slot, 1, cu * kv_unit * 2, &dk)) != cudaSuccess ||
-            (e = pool.reserve(slot, 2, cu * v_unit * 2, &dv)) != cudaSuccess ||
+        if (kvbuf < 0) {
+            e = pool.reserve(slot, 1, cu * kv_unit * 2, &dk);
+            if (e == cudaSuccess) e = pool.reserve(slot, 2, cu * v_unit * 2, &dv);
+        } else {
+            e = pool.reserve_kv(kvbuf, 0, kv_unit * 2, &dk);
+            if (e == cudaSuccess) e = pool.reserve_kv(kvbuf, 1, v_unit * 2, &dv);
+        }
+        if (e != cudaSuccess || (e = pool.reserve(slot, 0, nh * q_head * 2, &dq)) != cudaSuccess ||
             (e = pool.reserve(slot, 3, nh * o_head * out_es, &dout)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
         if (p->lse && (e = pool.reserve(slot, 4, nh * M * sizeof(float), &dlse)) != cudaSuccess)
@@ -402,7 +443,8 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         const char* hv = static_cast<const char*>(p->v) + u0 * v_unit * in_es;
         struct Part { const char* src; void* dst; size_t elems; } parts[3] = {
             {hq, dq, nh * q_head}, {hk, dk, cu * kv_unit}, {hv, dv, cu * v_unit}};
-        for (const Part& part : parts) {
+        for (int pi = 0; pi < (kv_up ? 3 : 1); ++pi) {  // a unit's later pieces reuse its K/V
+            const Part& part = parts[pi];
             if (in_es == 2) {
                 e = cudaMemcpyAsync(part.dst, part.src, part.elems * 2, cudaMemcpyHostToDevice, st);
             } else {

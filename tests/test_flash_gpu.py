@@ -603,3 +603,37 @@ def test_device_status_clean_after_runs():
     import odf_b200
 
     assert odf_b200.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("mod,in_dtype", [("alibi", "bf16"), ("head_key_bias", "f32")])
+def test_host_entry_few_units_in_query_head_pieces(mod, in_dtype):
+    """Fewer than four (batch, kv-head) units (here 2 units of 8 query heads, N 9600): the host
+    entry cuts each unit into pieces of query heads that share one upload of the unit's K/V (the
+    shape one GPU gets when a GQA problem is split over several GPUs).  Per-piece ALiBi slopes,
+    bias planes and fp32 conversion included, the result equals the device entry bit for bit."""
+    import odf_b200
+
+    B, H, Hk, N, D = 1, 16, 2, 9600, 128
+    rng = np.random.default_rng(43)
+    q, k, v = (np.ascontiguousarray((rng.standard_normal((B, h, N, D)).astype(np.float32).view(np.uint32) >> 16)
+                                    .astype(np.uint16)) for h in (H, Hk, Hk))
+    if in_dtype == "f32":
+        hq, hk, hv = ((x.astype(np.uint32) << 16).view(np.float32) for x in (q, k, v))
+    else:
+        hq, hk, hv = q, k, v
+    kw, dkw = {}, {}
+    if mod == "alibi":
+        kw["alibi"] = dkw["alibi"] = True
+    else:
+        bias = rng.standard_normal((1, H, 1, N)).astype(np.float32)
+        kw["bias"], dkw["bias"] = bias, to_dev(bias, _torch().float32)
+    lse = np.empty((B, H, N), dtype=np.float32)
+    o, _ = odf_b200.flash_fwd_host(hq, hk, hv, causal=True, lse_out=lse, **kw)
+    torch = _torch()
+    tq, tk, tv = (torch.from_numpy(x.astype(np.int16)).view(torch.bfloat16).cuda() for x in (q, k, v))
+    o_dev = torch.empty((B, H, N, D), dtype=torch.float32, device="cuda")
+    lse_dev = torch.empty((B, H, N), dtype=torch.float32, device="cuda")
+    odf_b200.flash_fwd(tq, tk, tv, causal=True, out=o_dev, lse_out=lse_dev, **dkw)
+    torch.cuda.synchronize()
+    assert np.array_equal(o, o_dev.cpu().numpy())
+    assert np.array_equal(lse, lse_dev.cpu().numpy())
