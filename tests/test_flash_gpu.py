@@ -637,3 +637,38 @@ def test_host_entry_few_units_in_query_head_pieces(mod, in_dtype):
     torch.cuda.synchronize()
     assert np.array_equal(o, o_dev.cpu().numpy())
     assert np.array_equal(lse, lse_dev.cpu().numpy())
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("mod", ["none", "alibi", "softcap", "alibi_softcap", "bias", "bias_softcap"])
+@pytest.mark.parametrize("masked", [False, True])
+def test_variant_matrix_gqa_ragged(d, causal, mod, masked):
+    """Every kernel instantiation (d, score mod) crossed with causal / non-causal and with a block
+    mask whose blocks do not line up with the 128x128 tiles, on GQA (4 q-heads over 2 kv-heads)
+    with M != N and ragged tile ends, against the oracle."""
+    import oracle
+
+    torch = _torch()
+    B, H, Hk, M, N = 1, 4, 2, 200, 330
+    q, k, v = make_qkv(200 + d + 7 * causal + 3 * masked, B, H, Hk, M, N, d, scale=1.3)
+    kw, okw = {"causal": causal}, {"causal": causal}
+    if "alibi" in mod:
+        kw["alibi"] = True
+        okw["alibi_slopes"] = oracle.alibi_slopes(H)
+    if "softcap" in mod:
+        kw["softcap"] = okw["softcap"] = 7.5
+    if mod.startswith("bias"):
+        bias = _bias(60 + d, (1, H, M, N), scale=1.5)
+        kw["bias"] = to_dev(bias, torch.float32)
+        okw["bias"] = bias
+    if masked:
+        rng = np.random.default_rng(61 + d)
+        mb = (48, 80)
+        mask = (rng.random((-(-M // mb[0]), -(-N // mb[1]))) > 0.3).astype(np.uint8)
+        mask[:, 0] = 1  # every query block sees at least one key block
+        kw.update(block_mask=mask, mask_block=mb)
+        okw.update(mask=mask, mask_block=mb)
+    o, lse = run_gpu(q, k, v, **kw)
+    o_ref, lse_ref = oracle_fwd(q, k, v, **okw)
+    check_close(o, lse, o_ref, lse_ref, f"d={d} causal={causal} {mod} masked={masked}")
