@@ -9,8 +9,9 @@
 
 namespace odf {
 
-// 2^x for a pair on the FMA pipe.  At d = 64 the MUFU unit (16 ex2 per clock per SM) is the
-// binding limit, so part of the columns take this path instead.  x is clamped to -127, split as
+// 2^x for a pair on the FMA pipe.  At d = 64, and in the soft-capped variants whose MUFU unit
+// also computes tanh, the MUFU unit (16 results per clock per SM) is the binding limit, so part
+// of the columns take this path instead.  x is clamped to -127, split as
 // x = j + f with j = rint(x) (by adding and subtracting 1.5 * 2^23) and f in [-0.5, 0.5]; 2^f
 // comes from a degree-3 polynomial whose coefficients were fitted here for minimax relative
 // error with p(0) = 1 (max relative error 1.0e-4), and j is added to the exponent field.
