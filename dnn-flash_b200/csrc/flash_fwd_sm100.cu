@@ -823,12 +823,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t scale2 = ptx::f32x2(args.scale * args.inv_softcap);
                     const uint64_t slope2 = ptx::f32x2(slope * args.inv_softcap);
                     const uint64_t sb2 = ptx::f32x2(slope * base * args.inv_softcap);
+                    // column indices (c, c + 1) as floats, stepped in four exact chains instead of
+                    // materialising 64 constant pairs
+                    uint64_t cidx[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) cidx[k] = ptx::f32x2(2.0f * k, 2.0f * k + 1.0f);
 #pragma unroll
                     for (int c = 0; c < 128; c += 2) {
                         uint64_t x = ptx::f32x2(s[c], s[c + 1]);
                         if (MOD & kModAlibi) {
-                            const uint64_t bias = ptx::ffma2(ptx::f32x2(static_cast<float>(c), static_cast<float>(c + 1)),
-                                                             slope2, sb2);
+                            uint64_t& ci = cidx[(c >> 1) & 3];
+                            const uint64_t bias = ptx::ffma2(ci, slope2, sb2);
+                            ci = ptx::fadd2(ci, ptx::f32x2(8.0f));
                             x = ptx::ffma2(x, scale2, bias);
                         } else if (MOD & kModBias) {  // the bias pass left s * scale + bias
                             x = ptx::fmul2(x, ptx::f32x2(args.inv_softcap));
@@ -840,10 +846,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                         s[c + 1] = ptx::hi_f32(y);
                     }
                 } else if (MOD & kModAlibi) {
+                    // s * scale * log2(e) + slope * log2(e) * (base + c) on pairs: base + c (exact for the
+                    // integer-valued columns) is stepped in four chains, then one multiply and one FMA
                     const float base = static_cast<float>(k0 - qi);
+                    const uint64_t scale2 = ptx::f32x2(args.scale_log2);
+                    const uint64_t slope2 = ptx::f32x2(slope_log2);
+                    uint64_t col[4];
 #pragma unroll
-                    for (int c = 0; c < 128; ++c) {
-                        s[c] = fmaf(s[c], args.scale_log2, slope_log2 * (base + static_cast<float>(c)));
+                    for (int k = 0; k < 4; ++k) col[k] = ptx::f32x2(base + 2.0f * k, base + 2.0f * k + 1.0f);
+#pragma unroll
+                    for (int c = 0; c < 128; c += 2) {
+                        uint64_t& ck = col[(c >> 1) & 3];
+                        const uint64_t y = ptx::ffma2(ptx::f32x2(s[c], s[c + 1]), scale2, ptx::fmul2(slope2, ck));
+                        ck = ptx::fadd2(ck, ptx::f32x2(8.0f));
+                        s[c] = ptx::lo_f32(y);
+                        s[c + 1] = ptx::hi_f32(y);
                     }
                 } else if (!raw && !(MOD & kModBias)) {
 #pragma unroll
