@@ -569,6 +569,12 @@ def test_host_entry_split_first_and_last_units(mod, in_dtype):
     kw, dkw = {}, {}
     if mod == "alibi":
         kw["alibi"] = dkw["alibi"] = True
+    elif mod == "block_mask":
+        import oracle
+
+        mask = oracle.sliding_window_prefix_mask(N // 128, 6, 3)
+        kw.update(block_mask=mask, mask_block=(128, 128))
+        dkw.update(block_mask=mask, mask_block=(128, 128))
     else:
         bias = rng.standard_normal((1, H, 1, N)).astype(np.float32)
         kw["bias"], dkw["bias"] = bias, to_dev(bias, _torch().float32)
@@ -605,7 +611,7 @@ def test_device_status_clean_after_runs():
     assert odf_b200.device_status(clear=True) == 0
 
 
-@pytest.mark.parametrize("mod,in_dtype", [("alibi", "bf16"), ("head_key_bias", "f32")])
+@pytest.mark.parametrize("mod,in_dtype", [("alibi", "bf16"), ("head_key_bias", "f32"), ("block_mask", "bf16")])
 def test_host_entry_few_units_in_query_head_pieces(mod, in_dtype):
     """Fewer than four (batch, kv-head) units (here 2 units of 8 query heads, N 9600): the host
     entry cuts each unit into pieces of query heads that share one upload of the unit's K/V (the
@@ -624,6 +630,12 @@ def test_host_entry_few_units_in_query_head_pieces(mod, in_dtype):
     kw, dkw = {}, {}
     if mod == "alibi":
         kw["alibi"] = dkw["alibi"] = True
+    elif mod == "block_mask":
+        import oracle
+
+        mask = oracle.sliding_window_prefix_mask(N // 128, 6, 3)
+        kw.update(block_mask=mask, mask_block=(128, 128))
+        dkw.update(block_mask=mask, mask_block=(128, 128))
     else:
         bias = rng.standard_normal((1, H, 1, N)).astype(np.float32)
         kw["bias"], dkw["bias"] = bias, to_dev(bias, _torch().float32)
