@@ -54,6 +54,13 @@ CONFIGS = {
                          in_scale=1.0, out="bf16", mask=None),
     "mha8k_dense": dict(B=2, Hq=32, Hkv=32, N=8192, D=128, causal=False, alibi=False, softcap=0.0,
                         in_scale=1.0, out="bf16", mask=None),
+    # The same-shape additive bias (BiasKind::SameShapeTile) on the north-star shape: one fp32 [N, N]
+    # matrix shared by every (batch, head) (tensor-bound), and a full fp32 [B, H, N, N] tensor, whose
+    # reads dominate the bytes (HBM-bound).
+    "bias8k": dict(B=2, Hq=32, Hkv=32, N=8192, D=128, causal=True, alibi=False, softcap=0.0, in_scale=1.0,
+                   out="bf16", mask=None, bias="broadcast"),
+    "bias8k_full": dict(B=1, Hq=16, Hkv=16, N=8192, D=128, causal=True, alibi=False, softcap=0.0, in_scale=1.0,
+                        out="bf16", mask=None, bias="full"),
 }
 WORKLOAD_NAMES = {
     "c1": "c1_mha_noncausal_b1h4_n512_d64",
@@ -63,6 +70,8 @@ WORKLOAD_NAMES = {
     "c5": "c5_gqa_causal_hq64_hkv8_n32768_d128",
     "mha8k_causal": "mha_causal_b2h32_n8192_d128",
     "mha8k_dense": "mha_dense_b2h32_n8192_d128",
+    "bias8k": "bias_broadcast_nxn_causal_b2h32_n8192_d128",
+    "bias8k_full": "bias_full_bhnn_causal_b1h16_n8192_d128",
 }
 
 
@@ -76,6 +85,17 @@ def block_mask_for(cfg):
     qb = np.arange(cfg["N"] // 128)[:, None]
     kb = np.arange(cfg["N"] // 128)[None, :]
     return ((kb <= qb) & ((qb - kb < 4) | (kb < 4))).astype(np.uint8)
+
+
+def unmasked_pairs(cfg):
+    """#unmasked (query, key) pairs of one (batch, q-head)."""
+    return flop_per_unit_pairs(cfg) // (4 * cfg["D"])
+
+
+def bias_planes(cfg):
+    """fp32 bias planes the config reads: 0 (no bias), 1 (one [N, N] matrix for all), B * Hq (full)."""
+    kind = cfg.get("bias")
+    return 0 if kind is None else (1 if kind == "broadcast" else cfg["B"] * cfg["Hq"])
 
 
 def flop_per_unit_pairs(cfg):
@@ -325,6 +345,9 @@ def cpu_reference_sample(cfg, rows, steps, warmup, use_ref=True):
         kind = "port"  # the reference has no soft-cap
     if kind == "port":
         kw["softcap"] = cfg["softcap"]
+    if cfg.get("bias"):  # the reference's ScoreBiasFn path reads the same values
+        shape = (1, 1, R, R) if cfg["bias"] == "broadcast" else (B, Hq, R, R)
+        kw["bias"] = rng.standard_normal(shape).astype(np.float32)
     sub = dict(cfg, N=R, mask=None)
     flop = flop_per_unit_pairs(sub) * B * Hq
     times = []
@@ -464,6 +487,10 @@ def run_ours(args, cfg, workload):
     o = torch.empty((B, Hq, N, D), dtype=out_dtype, device=dev)
     lse = torch.empty((B, Hq, N), dtype=torch.float32, device=dev)
     mask = block_mask_for(cfg)
+    bias = None
+    if cfg.get("bias"):
+        bshape = (1, 1, N, N) if cfg["bias"] == "broadcast" else (B, Hq, N, N)
+        bias = torch.randn(bshape, generator=g, device=dev)
     flop_rank = flop_per_unit_pairs(cfg) * B * Hq
     launches_per_step = 2 if mask is not None else 1
 
@@ -471,11 +498,12 @@ def run_ours(args, cfg, workload):
 
     def step():
         odf_b200.flash_fwd(q, k, v, causal=cfg["causal"], alibi=cfg["alibi"], softcap=cfg["softcap"],
-                           block_mask=mask, out=o, lse_out=lse)
+                           block_mask=mask, out=o, lse_out=lse, bias=bias)
 
     # algorithmic bytes: Q, K, V read once, O and LSE written once
     out_es = 2 if out_dtype == torch.bfloat16 else 4
     alg_bytes = (B * Hq * N * D * 2 + 2 * B * Hkv * N * D * 2 + B * Hq * N * D * out_es + B * Hq * N * 4)
+    alg_bytes += unmasked_pairs(cfg) * 4 * bias_planes(cfg)  # the bias values the mask keeps, read once
     # Working sets under twice the 126 MB L2 get an L2 flush (a 256 MB write) between timed steps;
     # the value then sums the per-step event times, which exclude the flushes.
     l2_bytes = 126 * 2 ** 20
@@ -535,10 +563,12 @@ def run_ours(args, cfg, workload):
     hqn, hkn, hvn = (t.view(torch.int16).numpy().view(np.uint16) for t in (hq, hk, hv))
     hon = ho.view(torch.int16).numpy().view(np.uint16) if out_dtype == torch.bfloat16 else ho.numpy()
     hln = hl.numpy()
+    hb = bias.cpu().pin_memory() if bias is not None else None
+    hbn = hb.numpy() if hb is not None else None
 
     def e2e_step():
         odf_b200.flash_fwd_host(hqn, hkn, hvn, causal=cfg["causal"], alibi=cfg["alibi"], softcap=cfg["softcap"],
-                                block_mask=mask, out=hon, lse_out=hln)
+                                block_mask=mask, out=hon, lse_out=hln, bias=hbn)
 
     e2e_step()  # warm the host-entry pool
     if dist:
@@ -548,7 +578,7 @@ def run_ours(args, cfg, workload):
         e2e_step()
     e2e_s = (time.perf_counter() - t0) / e2e_steps
     os.sched_setaffinity(0, saved_affinity)
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv) + ((hb,) if hb is not None else ()))
     d2h = ho.numel() * ho.element_size() + hl.numel() * 4
 
     total_ms, e2e_s = reduce_max([total_ms, e2e_s], dist)
@@ -557,7 +587,7 @@ def run_ours(args, cfg, workload):
     value = world * flop_rank * args.steps / (total_ms * 1e-3) / 1e12  # every rank runs the same FLOP
     avg_launch_ms = statistics.mean(per_launch_ms)
     achieved = flop_rank / (avg_launch_ms * 1e-3) / 1e12
-    mod = (1 if cfg["alibi"] else 0) | (2 if cfg["softcap"] > 0 else 0)
+    mod = (1 if cfg["alibi"] else 0) | (2 if cfg["softcap"] > 0 else 0) | (4 if cfg.get("bias") else 0)
     if mod == 0 and D == 128 and cfg["mask"] is None and -(-N // 128) >= 48:
         mod = 8  # the library's launch picks the variant that skips the row-max pass (kModSkipMax)
     if flop_rank / alg_bytes >= peak * 1e12 / (hbm * 1e9):  # above the ridge point: tensor-bound
@@ -593,7 +623,7 @@ def run_ours(args, cfg, workload):
                 "batch_per_gpu": B, "global_batch": B * world if args.scaling == "weak" else CONFIGS[args.config]["B"],
                 "heads_q_per_gpu": Hq, "heads_kv_per_gpu": Hkv, "seq_len": N,
                 "head_dim": D, "causal": cfg["causal"], "alibi": cfg["alibi"], "softcap": cfg["softcap"],
-                "block_mask": cfg["mask"], "out_dtype": cfg["out"], "lse": True,
+                "block_mask": cfg["mask"], "bias": cfg.get("bias"), "out_dtype": cfg["out"], "lse": True,
                 "parallelism": f"(batch x head) shards, {world} GPU(s), no collective on the data path",
                 "flop_per_gpu_step": flop_rank,
                 "l2": l2_note,

@@ -236,6 +236,9 @@ struct HostPool {
     static constexpr int kSplitUnits = 3;
     void* kvd[kSplitUnits][2] = {};
     size_t kvd_cap[kSplitUnits][2] = {};
+    // A same-shape bias broadcast over batch and heads: one plane, uploaded once per call.
+    void* shared_bias = nullptr;
+    size_t shared_bias_cap = 0;
     ~HostPool() {
         // Process teardown may run after the CUDA context is gone; freeing is best-effort.
         for (auto& set : buf)
@@ -245,11 +248,24 @@ struct HostPool {
         for (auto& pair : kvd)
             for (void*& b : pair)
                 if (b) cudaFree(b);
+        if (shared_bias) cudaFree(shared_bias);
         for (auto* evs : {in_done, comp_done, out_done})
             for (int i = 0; i < kHostSets; ++i)
                 if (evs[i]) cudaEventDestroy(evs[i]);
         for (auto& s : streams)
             if (s) cudaStreamDestroy(s);
+    }
+    cudaError_t reserve_shared_bias(size_t bytes, void** out) {
+        if (shared_bias_cap < bytes) {
+            if (shared_bias) cudaFree(shared_bias);
+            shared_bias = nullptr;
+            shared_bias_cap = 0;
+            cudaError_t e = cudaMalloc(&shared_bias, bytes);
+            if (e != cudaSuccess) return e;
+            shared_bias_cap = bytes;
+        }
+        *out = shared_bias;
+        return cudaSuccess;
     }
     cudaError_t reserve_kv(int which, int idx, size_t bytes, void** out) {
         if (kvd_cap[which][idx] < bytes) {
@@ -414,20 +430,20 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         if (c >= kHostSets && (e = cudaStreamWaitEvent(s_in, pool.comp_done[slot], 0)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
         // Same-shape bias: the footprint of each (batch, q-head) plane of this chunk, copied to a
-        // device staging buffer with the row/key strides kept (one plane when the bias is
-        // broadcast over batch and heads).
+        // device staging buffer with the row/key strides kept.  A bias broadcast over batch and
+        // heads is one plane for every chunk: it is uploaded once, by the first chunk.
         const float* dbias = nullptr;
         int64_t bias_plane = 0;
         if (p->bias_kind == ODF_BIAS_SAME_SHAPE) {
             const int64_t* bs = r.bs;
             const int64_t foot = (M - 1) * bs[2] + (N - 1) * bs[3] + 1;
             const bool shared = bs[0] == 0 && bs[1] == 0;
-            const int64_t planes = shared ? 1 : nh;
+            const int64_t planes = shared ? (c == 0 ? 1 : 0) : nh;
             bias_plane = shared ? 0 : (foot + 3) / 4 * 4;
             void* db = nullptr;
-            if ((e = pool.reserve(slot, 7, static_cast<size_t>(shared ? foot : planes * bias_plane) * sizeof(float),
-                                  &db)) != cudaSuccess)
-                return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+            e = shared ? pool.reserve_shared_bias(static_cast<size_t>(foot) * sizeof(float), &db)
+                       : pool.reserve(slot, 7, static_cast<size_t>(planes * bias_plane) * sizeof(float), &db);
+            if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
             for (int64_t j = 0; j < planes && e == cudaSuccess; ++j) {
                 const int64_t gh = h0 + j;  // global (batch, q-head) index of this plane
                 const int64_t b = gh / p->heads_q, h = gh % p->heads_q;
