@@ -684,3 +684,18 @@ def test_variant_matrix_gqa_ragged(d, causal, mod, masked):
     o, lse = run_gpu(q, k, v, **kw)
     o_ref, lse_ref = oracle_fwd(q, k, v, **okw)
     check_close(o, lse, o_ref, lse_ref, f"d={d} causal={causal} {mod} masked={masked}")
+
+
+@pytest.mark.parametrize("m", [1, 16, 300])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("want_lse", [True, False])
+def test_few_query_rows_long_keys(m, causal, want_lse):
+    """Decode- and prefill-shaped problems: a few query rows against 8192 keys (GQA 8 over 2, d=128),
+    which run the long-range variant (64 KV tiles) with one partial query tile; causal stays
+    top-left aligned (row qi sees keys 0..qi).  O (and LSE when asked for) against the oracle;
+    without an LSE buffer the kernel writes none."""
+    q, k, v = make_qkv(300 + m + 2 * causal, 1, 8, 2, m, 8192, 128)
+    o, lse = run_gpu(q, k, v, causal=causal, want_lse=want_lse)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=causal)
+    assert (lse is None) == (not want_lse)
+    check_close(o, lse, o_ref, lse_ref if want_lse else None, f"m={m} causal={causal}")
