@@ -82,6 +82,10 @@ constexpr float kLn2 = 0.6931471805599453f;
 // The running max is only raised when a tile's max exceeds it by more than this
 // (log2 units), so P stays below 2^8 and O is rescaled rarely.
 constexpr float kRescaleLog2 = 8.0f;
+// ALiBi far tiles: a tile whose every score is below the running max by more than this (log2
+// units) contributes P < 2^-48 per element, i.e. less than n * 2^-48 of l (l >= 1) over a row of
+// n keys, far below fp32 resolution: its P is written as zeros without the exponentials.
+constexpr float kFarLog2 = 48.0f;
 
 // Score-mod variants: ALiBi and the same-shape bias are exclusive (one BiasKind per call).
 // kModSkipMax marks the plain-score variant for long KV ranges whose unmasked tiles skip the
@@ -145,8 +149,11 @@ __device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, int pair, int j, 
     if (a.mode == kModeList) return __ldg(a.tile_list + static_cast<int64_t>(pair) * a.n_kt + j);
     uint32_t e = static_cast<uint32_t>(j);
     if (a.mode == kModeCausal) {
-        if (j * kTileK < qend0) e |= kNeed0;
-        if (valid1 && j * kTileK < qend1) e |= kNeed1;
+        // the pair's tiles 0 .. n_e - 1, in reverse with kv_reverse (diagonal first)
+        const int kt = a.kv_reverse ? min(a.n_kt, (qend1 + kTileK - 1) / kTileK) - 1 - j : j;
+        e = static_cast<uint32_t>(kt);
+        if (kt * kTileK < qend0) e |= kNeed0;
+        if (valid1 && kt * kTileK < qend1) e |= kNeed1;
     } else {
         e |= kNeed0;
         if (valid1) e |= kNeed1;
@@ -224,6 +231,14 @@ __device__ __forceinline__ int64_t static_item(int64_t n_items, int it) {
     const int64_t c = (it & 1) ? (g - 1 - blockIdx.x) : blockIdx.x;
     const int64_t k = static_cast<int64_t>(it) * g + c;
     return k < n_items ? k : -1;
+}
+
+// P = 0 over a far tile's 128 keys (64 columns of bf16 pairs), ready for the P.V MMA once the
+// caller arrives on p_full.
+__device__ __forceinline__ void store_zero_p(uint32_t p_addr) {
+    ptx::tmem_st64_zero_nowait(p_addr);
+    ptx::tmem_st_wait();
+    ptx::tc_fence_before();
 }
 
 // Bits of the 128 columns [k0, k0+128) that the BlockMask allows for query row qi
@@ -647,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     r.n_iter = I.n_entries;
                 } else if (!valid) {
                     r.n_iter = 0;
-                } else if (args.mode == kModeCausal) {  // tiles j with j * 128 < row end (as kv_entry)
+                } else if (args.mode == kModeCausal && !args.kv_reverse) {  // tiles j with j * 128 < row end
                     r.n_iter = min(I.n_entries, ((qtile == 0 ? I.qend0 : I.qend1) + kTileK - 1) / kTileK);
                 } else {
                     r.n_iter = I.n_entries;
@@ -674,6 +689,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n_iter = rec->n_iter;
             for (int j = 0; j < n_iter; ++j) {
                 uint32_t e = static_cast<uint32_t>(j) | need_bit;
+                if (args.kv_reverse) {  // causal, diagonal first: entry j is tile n_entries - 1 - j
+                    const int kt_r = rec->n_entries - 1 - j;
+                    if (kt_r * kTileK >= min(args.m, rec->q0 + kTileQ)) continue;  // beyond this tile's rows
+                    e = static_cast<uint32_t>(kt_r) | need_bit;
+                }
                 if (args.mode == kModeList) {
                     e = __ldg(args.tile_list + static_cast<int64_t>(rec->pair) * args.n_kt + j);
                     if (!(e & need_bit)) continue;
@@ -828,22 +848,53 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint64_t cidx[4];
 #pragma unroll
                     for (int k = 0; k < 4; ++k) cidx[k] = ptx::f32x2(2.0f * k, 2.0f * k + 1.0f);
+                    if constexpr ((MOD & kModAlibi) != 0 && !Cfg::kSepP) {
+                        // t first, with its row max: tanh is monotone, so softcap * log2(e) * tanh(max t)
+                        // bounds the row's scores (masked and ragged columns only raise it), and a
+                        // far tile (every row below its running max by kFarLog2) skips tanh and ex2
+                        float tmax4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                    for (int c = 0; c < 128; c += 2) {
-                        uint64_t x = ptx::f32x2(s[c], s[c + 1]);
-                        if (MOD & kModAlibi) {
+                        for (int c = 0; c < 128; c += 2) {
                             uint64_t& ci = cidx[(c >> 1) & 3];
                             const uint64_t bias = ptx::ffma2(ci, slope2, sb2);
                             ci = ptx::fadd2(ci, ptx::f32x2(8.0f));
-                            x = ptx::ffma2(x, scale2, bias);
-                        } else if (MOD & kModBias) {  // the bias pass left s * scale + bias
-                            x = ptx::fmul2(x, ptx::f32x2(args.inv_softcap));
-                        } else {
-                            x = ptx::fmul2(x, scale2);
+                            const uint64_t x = ptx::ffma2(ptx::f32x2(s[c], s[c + 1]), scale2, bias);
+                            s[c] = ptx::lo_f32(x);
+                            s[c + 1] = ptx::hi_f32(x);
+                            tmax4[(c >> 1) & 3] = ptx::fmax3(tmax4[(c >> 1) & 3], s[c], s[c + 1]);
                         }
-                        const uint64_t y = tanh2(x);
-                        s[c] = ptx::lo_f32(y);
-                        s[c + 1] = ptx::hi_f32(y);
+                        const float bound =
+                            fold * ptx::tanh_approx(fmaxf(fmaxf(tmax4[0], tmax4[1]), fmaxf(tmax4[2], tmax4[3])));
+                        if (__all_sync(0xffffffffu, m_run != -INFINITY && bound < m_run - kFarLog2)) {
+                            store_zero_p(p_addr);
+                            ptx::mbar_arrive(&bars.p_full[qtile]);
+                            phases = (phases ^ 1u) | 4u;
+                            continue;
+                        }
+#pragma unroll
+                        for (int c = 0; c < 128; c += 2) {
+                            const uint64_t y = tanh2(ptx::f32x2(s[c], s[c + 1]));
+                            s[c] = ptx::lo_f32(y);
+                            s[c + 1] = ptx::hi_f32(y);
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 128; c += 2) {
+                            uint64_t x = ptx::f32x2(s[c], s[c + 1]);
+                            if (MOD & kModAlibi) {
+                                uint64_t& ci = cidx[(c >> 1) & 3];
+                                const uint64_t bias = ptx::ffma2(ci, slope2, sb2);
+                                ci = ptx::fadd2(ci, ptx::f32x2(8.0f));
+                                x = ptx::ffma2(x, scale2, bias);
+                            } else if (MOD & kModBias) {  // the bias pass left s * scale + bias
+                                x = ptx::fmul2(x, ptx::f32x2(args.inv_softcap));
+                            } else {
+                                x = ptx::fmul2(x, scale2);
+                            }
+                            const uint64_t y = tanh2(x);
+                            s[c] = ptx::lo_f32(y);
+                            s[c + 1] = ptx::hi_f32(y);
+                        }
                     }
                 } else if (MOD & kModAlibi) {
                     // s * scale * log2(e) + slope * log2(e) * (base + c) on pairs: base + c (exact for the
@@ -899,6 +950,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float tile_max = ptx::fmax3(ptx::fmax3(mx8[0], mx8[1], mx8[2]), ptx::fmax3(mx8[3], mx8[4], mx8[5]),
                                             fmaxf(mx8[6], mx8[7]));
                 if (raw || (MOD & kModSoftcap)) tile_max *= fold;
+                if constexpr ((MOD & kModAlibi) != 0 && (MOD & kModSoftcap) == 0 && !Cfg::kSepP) {
+                    // ALiBi far tile: every row's max below its running max by kFarLog2
+                    if (__all_sync(0xffffffffu, m_run != -INFINITY && tile_max < m_run - kFarLog2)) {
+                        store_zero_p(p_addr);
+                        ptx::mbar_arrive(&bars.p_full[qtile]);
+                        phases = (phases ^ 1u) | 4u;
+                        continue;
+                    }
+                }
                 float alpha = 1.0f;
                 if (m_run == -INFINITY) {
                     m_run = tile_max;  // first valid tile of this row: O holds zeros so far

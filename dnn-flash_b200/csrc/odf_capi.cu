@@ -165,6 +165,8 @@ odf::FwdLaunch make_launch(const odf_fwd_params* p, const Resolved& r) {
     a.n_kt = r.n_kt;
     a.causal = p->causal != 0;
     a.mode = p->block_mask ? odf::kModeList : (p->causal ? odf::kModeCausal : odf::kModeDense);
+    // causal ALiBi at d = 128: diagonal tile first, so far tiles meet a settled running max
+    a.kv_reverse = a.mode == odf::kModeCausal && p->bias_kind == ODF_BIAS_ALIBI && p->head_dim == 128;
     a.scale = p->scale;
     a.scale_log2 = p->scale * 1.4426950408889634f;
     a.softcap = p->softcap;

@@ -37,6 +37,9 @@ struct FwdArgs {
     int32_t n_qt, n_kt, n_pairs;
     int32_t mode;
     int32_t causal;
+    // Causal mode only: an item walks its KV tiles from the diagonal down to tile 0 (set for
+    // ALiBi at d = 128, whose nearest keys carry the row's largest scores).
+    int32_t kv_reverse;
     float scale;        // natural-units softmax scale
     float scale_log2;   // scale * log2(e)
     float softcap;      // 0 = off

@@ -303,6 +303,11 @@ __device__ __forceinline__ void tmem_st64_nowait(uint32_t taddr, const uint32_t*
     asm volatile("tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};" ::"r"(taddr), "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]), "r"(u[8]), "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15]), "r"(u[16]), "r"(u[17]), "r"(u[18]), "r"(u[19]), "r"(u[20]), "r"(u[21]), "r"(u[22]), "r"(u[23]), "r"(u[24]), "r"(u[25]), "r"(u[26]), "r"(u[27]), "r"(u[28]), "r"(u[29]), "r"(u[30]), "r"(u[31]), "r"(u[32]), "r"(u[33]), "r"(u[34]), "r"(u[35]), "r"(u[36]), "r"(u[37]), "r"(u[38]), "r"(u[39]), "r"(u[40]), "r"(u[41]), "r"(u[42]), "r"(u[43]), "r"(u[44]), "r"(u[45]), "r"(u[46]), "r"(u[47]), "r"(u[48]), "r"(u[49]), "r"(u[50]), "r"(u[51]), "r"(u[52]), "r"(u[53]), "r"(u[54]), "r"(u[55]), "r"(u[56]), "r"(u[57]), "r"(u[58]), "r"(u[59]), "r"(u[60]), "r"(u[61]), "r"(u[62]), "r"(u[63]) : "memory");
 }
 
+// Zeros -> 32 lanes x 64 columns of TMEM (one zero register for every column; not waited).
+__device__ __forceinline__ void tmem_st64_zero_nowait(uint32_t taddr) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(0u) : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- math

@@ -198,6 +198,21 @@ def test_generated_alibi_slopes_beyond_256_heads(softcap):
     check_close(o, lse, o_ref, lse_ref, f"generated slopes, 320 heads, softcap {softcap}")
 
 
+@pytest.mark.parametrize("m,n", [(1000, 1000), (300, 700), (700, 300), (129, 129)])
+@pytest.mark.parametrize("softcap", [0.0, 20.0])
+def test_causal_alibi_far_tiles_diagonal_first(m, n, softcap):
+    """Causal ALiBi at d = 128 walks each query tile's KV tiles from the diagonal down to tile 0,
+    and a tile whose scores all lie 48 (log2) below the running max writes P = 0 without the
+    exponentials.  Steep slopes make most tiles far; GQA, ragged ends and M != N (top-left causal)
+    cross the pair and row bookkeeping of the reversed walk."""
+    H, Hk = 4, 2
+    slopes = np.array([4.0, 1.0, 0.25, 0.0625], dtype=np.float32)
+    q, k, v = make_qkv(61, 2, H, Hk, m, n, 128)
+    o, lse = run_gpu(q, k, v, causal=True, alibi=True, alibi_slopes=slopes, softcap=softcap)
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, alibi_slopes=slopes, softcap=softcap)
+    check_close(o, lse, o_ref, lse_ref, f"far tiles m={m} n={n} softcap={softcap}")
+
+
 def test_explicit_alibi_slopes_and_noncausal_scale():
     H = 3
     slopes = np.array([0.5, 0.03125, 0.25], dtype=np.float32)
