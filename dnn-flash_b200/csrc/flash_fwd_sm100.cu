@@ -313,6 +313,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars.drain = bars.item_empty + kItemQueue;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars.drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    // [2][4] bytes: softmax warp w of query tile i wrote its last P as zeros (an ALiBi far tile);
+    // when all four did, the MMA warp leaves out that tile's P.V
+    volatile uint8_t* far_flags = reinterpret_cast<volatile uint8_t*>(tmem_slot + 2);
+    constexpr bool kFarSkip = (MOD & kModAlibi) != 0 && !Cfg::kSepP;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -342,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::mbar_init(bars.drain, 1);
         *abort_flag = 0;
+        for (int i = 0; i < 8; ++i) far_flags[i] = 0;
         ptx::fence_barrier_init();
         ptx::fence_proxy_async_smem();
     }
@@ -481,6 +486,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns))
                         return false;
                     ptx::tc_fence_after();
+                    if (kFarSkip && acc[i] &&
+                        *reinterpret_cast<volatile const uint32_t*>(far_flags + 4 * i) == 0x01010101u) {
+                        ++pv_count[i];  // P_i is zero in all 128 rows: O_i stays as it is
+                        return true;
+                    }
                     const uint32_t vd = v_lo0 + static_cast<uint32_t>(slot) * kSlotStep;
                     const uint32_t first = acc[i] ? 1u : 0u;
 #pragma unroll
@@ -867,6 +877,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             fold * ptx::tanh_approx(fmaxf(fmaxf(tmax4[0], tmax4[1]), fmaxf(tmax4[2], tmax4[3])));
                         if (__all_sync(0xffffffffu, m_run != -INFINITY && bound < m_run - kFarLog2)) {
                             store_zero_p(p_addr);
+                            if (lane == 0) far_flags[qtile * 4 + wq] = 1;
                             ptx::mbar_arrive(&bars.p_full[qtile]);
                             phases = (phases ^ 1u) | 4u;
                             continue;
@@ -954,6 +965,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // ALiBi far tile: every row's max below its running max by kFarLog2
                     if (__all_sync(0xffffffffu, m_run != -INFINITY && tile_max < m_run - kFarLog2)) {
                         store_zero_p(p_addr);
+                        if (lane == 0) far_flags[qtile * 4 + wq] = 1;
                         ptx::mbar_arrive(&bars.p_full[qtile]);
                         phases = (phases ^ 1u) | 4u;
                         continue;
@@ -1023,6 +1035,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::tmem_st64_nowait(p_addr, reinterpret_cast<const uint32_t*>(s));
                 ptx::tmem_st_wait();
                 ptx::tc_fence_before();
+                if (kFarSkip && lane == 0) far_flags[qtile * 4 + wq] = 0;
                 ptx::mbar_arrive(&bars.p_full[qtile]);
                 phases = (phases ^ 1u) | 4u;
             }
