@@ -134,7 +134,7 @@ struct Bars {
 // warp, written by lane 0) and read where needed, so that no registers stay tied up
 // across the softmax loop.
 struct RowItem {
-    int n_entries;  // KV tiles of the pair
+    int n_entries;  // KV tiles of the pair (reversed walk: up to and including the diagonal)
     int pair;
     int q0;         // first row of this warp's query tile
     int n_iter;     // list mode: n_entries; dense/causal: the KV tiles this query tile needs (0..n_iter-1)
@@ -166,7 +166,7 @@ struct Item {
     int bh, b, h, hk, pair;
     int q00, q01;      // first rows of Q0 and Q1
     int qend0, qend1;  // their row ends (clipped to M)
-    int n_entries;     // KV tiles visited by the pair
+    int n_entries;     // KV tiles visited by the pair (entries 0 .. n_entries - 1 of kv_entry)
     bool valid1;       // Q1 has rows
 };
 
@@ -210,6 +210,8 @@ __device__ __forceinline__ Item decode_item(const FwdArgs& a, int64_t k) {
         I.n_entries = a.tile_count[I.pair];
     } else if (a.mode == kModeCausal) {
         I.n_entries = min(a.n_kt, (I.qend1 + kTileK - 1) / kTileK);
+        // reversed walk: the tiles below kv_lo (far by the norm bound) are left out at its end
+        if (a.kv_lo != nullptr) I.n_entries -= __ldg(a.kv_lo + static_cast<int64_t>(I.bh) * a.n_pairs + I.pair);
     } else {
         I.n_entries = a.n_kt;
     }
@@ -664,7 +666,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) {
                 const Item I = decode_item(args, item);
                 RowItem r;
-                r.n_entries = I.n_entries;
+                // reversed walk: entry j is KV tile n_entries - 1 - j, counted from the top tile
+                r.n_entries = args.kv_reverse ? min(args.n_kt, (I.qend1 + kTileK - 1) / kTileK) : I.n_entries;
                 r.pair = I.pair;
                 r.q0 = qtile == 0 ? I.q00 : I.q01;
                 const bool valid = qtile == 0 || I.valid1;
@@ -1204,6 +1207,89 @@ __global__ void pair_list_kernel(int32_t m, int32_t n, int32_t n_pairs, int32_t 
     if (lane == 0) count[pair] = base;
 }
 
+// Largest row norm ||x_r||_2 of each 128-row tile of a bf16 [batch, heads, rows, 128] tensor
+// (element strides {b, h, t}, rows 16-byte aligned): one block of 128 threads per
+// (batch, head, tile), 16 lanes reading a row's 256 bytes.  Rows at or beyond `rows` count 0.
+__global__ void __launch_bounds__(128) tile_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t sb, int64_t sh,
+                                                        int64_t st, int32_t heads, int32_t rows, int32_t n_tiles,
+                                                        float* __restrict__ out) {
+    const int64_t idx = blockIdx.x;
+    const int tile = static_cast<int>(idx % n_tiles);
+    const int64_t bh = idx / n_tiles;
+    const int64_t b = bh / heads;
+    const int64_t h = bh - b * heads;
+    const __nv_bfloat16* base = x + b * sb + h * sh;
+    const int sub = threadIdx.x & 15;
+    float best = 0.0f;
+#pragma unroll 4
+    for (int r = threadIdx.x >> 4; r < kTileQ; r += 8) {
+        const int row = tile * kTileQ + r;
+        float ss = 0.0f;
+        if (row < rows) {
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(row) * st) + sub);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float lo = __uint_as_float(w[i] << 16);
+                const float hi = __uint_as_float(w[i] & 0xFFFF0000u);
+                ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+            }
+        }
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        best = fmaxf(best, ss);
+    }
+    best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, 16));
+    __shared__ float warp_best[4];
+    if ((threadIdx.x & 31) == 0) warp_best[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0)
+        out[idx] = sqrtf(fmaxf(fmaxf(warp_best[0], warp_best[1]), fmaxf(warp_best[2], warp_best[3])));
+}
+
+// Far KV tiles of causal ALiBi, from norms alone: for row qi and key kj of KV tile kt,
+// |s scale| <= |scale| |q_i| |k_j| (Cauchy-Schwarz) bounds the score from above by
+//   U = c Kmax(kt) + slope (kt*128 + 127 - q0),   c = |scale| Qmax(qt) (1 + 2^-7)
+// and every row's max from below by its diagonal key (kj = qi, ALiBi term 0), L = -c Kmax(qt).
+// With f the soft-cap (or the identity), f(U) < f(L) - 48 ln 2 gives P < 2^-48 of the row's
+// largest term on the whole tile.  kv_lo[pair] is the first KV tile that is not far for both
+// query tiles of the pair (tiles below it are all far); the first KV tile not far stops the scan.
+// A query tile with rows at or beyond N (no diagonal key), a non-positive or non-finite slope,
+// or non-finite norms keeps every tile.
+__global__ void far_lo_kernel(const FwdArgs a, const float* __restrict__ qn, const float* __restrict__ kn,
+                              int32_t* __restrict__ kv_lo) {
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t n_bh = static_cast<int64_t>(a.batch) * a.heads_q;
+    if (idx >= n_bh * a.n_pairs) return;
+    const int64_t bh = idx / a.n_pairs;
+    const int pair = static_cast<int>(idx - bh * a.n_pairs);
+    const int b = static_cast<int>(bh / a.heads_q);
+    const int h = static_cast<int>(bh - static_cast<int64_t>(b) * a.heads_q);
+    const int hk = h / (a.heads_q / a.heads_kv);
+    const float slope = a.alibi_generated ? exp2f(-8.0f * static_cast<float>(h + 1) / static_cast<float>(a.heads_q))
+                                          : a.alibi_slopes[h];
+    const float* kn_u = kn + (static_cast<int64_t>(b) * a.heads_kv + hk) * a.n_kt;
+    const float thr = 48.0f * kLn2;
+    int lo = 0x7fffffff;
+    for (int qt = 2 * pair; qt <= 2 * pair + 1 && qt < a.n_qt; ++qt) {
+        const int q0 = qt * kTileQ;
+        const int qe = min(a.m, q0 + kTileQ);
+        int lo_q = 0;
+        const float c = fabsf(a.scale) * qn[bh * a.n_qt + qt] * (1.0f + 0.0078125f);
+        if (qe - 1 < a.n && slope > 0.0f && isfinite(slope) && isfinite(c)) {
+            const float L = -c * kn_u[qt];
+            const float fL = a.softcap > 0.0f ? a.softcap * tanhf(L / a.softcap) : L;
+            for (; lo_q < qt; ++lo_q) {
+                const float U = c * kn_u[lo_q] + slope * static_cast<float>(lo_q * kTileK + kTileK - 1 - q0);
+                const float fU = a.softcap > 0.0f ? a.softcap * tanhf(U / a.softcap) : U;
+                if (!(fU < fL - thr)) break;  // NaN keeps the tile
+            }
+        }
+        lo = min(lo, lo_q);
+    }
+    kv_lo[idx] = lo;
+}
+
 __global__ void convert_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, int64_t n) {
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 4;
     for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
@@ -1303,6 +1389,14 @@ size_t workspace_bytes_for(int64_t seqlen_q, int64_t seqlen_k, bool has_mask) {
     const size_t list = static_cast<size_t>(n_pairs * n_kt) * sizeof(uint32_t);
     const size_t count = static_cast<size_t>(n_pairs) * sizeof(int32_t);
     return kSchedBytes + ((list + 255) & ~static_cast<size_t>(255)) + ((count + 255) & ~static_cast<size_t>(255));
+}
+
+size_t far_bound_bytes(int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seqlen_q, int64_t seqlen_k) {
+    const int64_t n_qt = (seqlen_q + kTileQ - 1) / kTileQ;
+    const int64_t n_pairs = (n_qt + 1) / 2;
+    const int64_t n_kt = (seqlen_k + kTileK - 1) / kTileK;
+    auto up = [](int64_t bytes) { return static_cast<size_t>((bytes + 255) & ~int64_t{255}); };
+    return up(batch * heads_q * n_qt * 4) + up(batch * heads_kv * n_kt * 4) + up(batch * heads_q * n_pairs * 4);
 }
 
 void* current_context() {
@@ -1482,6 +1576,30 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
         }
         a.tile_list = list;
         a.tile_count = count;
+    }
+    // causal ALiBi: the norm bound over whole KV tiles, when the workspace has room for it
+    a.kv_lo = nullptr;
+    if (a.kv_reverse && L.workspace != nullptr &&
+        L.workspace_bytes >= kSchedBytes + far_bound_bytes(a.batch, a.heads_q, a.heads_kv, a.m, a.n)) {
+        uint8_t* ws = static_cast<uint8_t*>(L.workspace) + kSchedBytes;
+        const int64_t nq = static_cast<int64_t>(a.batch) * a.heads_q * a.n_qt;
+        const int64_t nk = static_cast<int64_t>(a.batch) * a.heads_kv * a.n_kt;
+        float* qn = reinterpret_cast<float*>(ws);
+        float* kn = reinterpret_cast<float*>(ws + ((nq * 4 + 255) & ~int64_t{255}));
+        int32_t* lo = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(kn) + ((nk * 4 + 255) & ~int64_t{255}));
+        tile_norm_kernel<<<static_cast<unsigned>(nq), 128, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(L.q), L.q_strides[0], L.q_strides[1], L.q_strides[2], a.heads_q, a.m,
+            a.n_qt, qn);
+        tile_norm_kernel<<<static_cast<unsigned>(nk), 128, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(L.k), L.k_strides[0], L.k_strides[1], L.k_strides[2], a.heads_kv, a.n,
+            a.n_kt, kn);
+        const int64_t n_lo = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;
+        far_lo_kernel<<<static_cast<unsigned>((n_lo + 127) / 128), 128, 0, stream>>>(a, qn, kn, lo);
+        if (cudaGetLastError() != cudaSuccess) {
+            *err = "far-tile bound kernel launch failed";
+            return ODF_ERR_CUDA;
+        }
+        a.kv_lo = lo;
     }
     int mod = (L.has_alibi ? kModAlibi : 0) | (L.has_softcap ? kModSoftcap : 0) | (L.has_bias ? kModBias : 0);
     // long KV ranges of a plain score: the variant whose unmasked tiles skip the row-max pass (on

@@ -130,6 +130,15 @@ int validate(const odf_fwd_params* p, bool host, Resolved* r) {
     return ODF_OK;
 }
 
+// Required workspace plus, for causal ALiBi at d = 128 (no block mask), the optional room for
+// its far-tile bound, for a launch of `batch` x `heads_q` query heads over `heads_kv` KV heads.
+size_t workspace_with_far_bound(const odf_fwd_params* p, int64_t batch, int64_t heads_q, int64_t heads_kv) {
+    size_t bytes = odf::workspace_bytes_for(p->seqlen_q, p->seqlen_k, p->block_mask != nullptr);
+    if (p->causal && p->block_mask == nullptr && p->bias_kind == ODF_BIAS_ALIBI && p->head_dim == 128)
+        bytes += odf::far_bound_bytes(batch, heads_q, heads_kv, p->seqlen_q, p->seqlen_k);
+    return bytes;
+}
+
 float generated_slope(int64_t h, int64_t heads) {
     return std::exp2(-8.0f * static_cast<float>(h + 1) / static_cast<float>(heads));
 }
@@ -309,7 +318,7 @@ int odf_flash_fwd_sm100(const odf_fwd_params* p, void* stream) {
 
 size_t odf_fwd_workspace_size(const odf_fwd_params* p) {
     if (p == nullptr) return 0;
-    return odf::workspace_bytes_for(p->seqlen_q, p->seqlen_k, p->block_mask != nullptr);
+    return workspace_with_far_bound(p, p->batch, p->heads_q, p->heads_kv);
 }
 
 int odf_flash_fwd_host(const odf_fwd_params* p) {
@@ -398,7 +407,8 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
         dmask = static_cast<const uint8_t*>(pool.mask);
     }
-    const size_t ws_bytes = odf::workspace_bytes_for(M, N, p->block_mask != nullptr);
+    // a chunk launches batch 1 over at most all query heads and all units
+    const size_t ws_bytes = workspace_with_far_bound(p, 1, p->batch * p->heads_q, units);
 
     for (int64_t c = 0; c < static_cast<int64_t>(plan.size()); ++c) {
         const int64_t u0 = plan[c].u0, cu = plan[c].cu, g0 = plan[c].g0, ng = plan[c].ng;

@@ -40,6 +40,9 @@ struct FwdArgs {
     // Causal mode only: an item walks its KV tiles from the diagonal down to tile 0 (set for
     // ALiBi at d = 128, whose nearest keys carry the row's largest scores).
     int32_t kv_reverse;
+    // With kv_reverse, optional [batch * heads_q, n_pairs]: the pair's KV tiles below this index
+    // are far for both of its query tiles by the norm bound (far_lo_kernel) and are not visited.
+    const int32_t* kv_lo;
     float scale;        // natural-units softmax scale
     float scale_log2;   // scale * log2(e)
     float softcap;      // 0 = off
@@ -112,5 +115,9 @@ void* current_context();
 int* device_status_ptr(int device);
 
 size_t workspace_bytes_for(int64_t seqlen_q, int64_t seqlen_k, bool has_mask);
+
+// Optional workspace bytes after workspace_bytes_for(..., false) that causal ALiBi at d = 128
+// uses for its far-tile bound (tile norms and the per-pair first visited KV tile).
+size_t far_bound_bytes(int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seqlen_q, int64_t seqlen_k);
 
 }  // namespace odf

@@ -95,6 +95,25 @@ def test_block_mask_needs_sizes_and_workspace():
     assert "smaller" in odf_b200.last_error()
 
 
+def test_workspace_room_for_causal_alibi_far_bound():
+    """Causal ALiBi at d = 128 asks for optional room after the 256-byte counter: per (batch,
+    q-head) query-tile norms, per (batch, kv-head) KV-tile norms and per (batch, q-head) pair
+    first KV tiles, int32/fp32 each, every array rounded up to 256 bytes.  Other shapes and
+    masks do not; a 256-byte workspace stays valid (the bound is then left out)."""
+    lib = odf_b200.load_library()
+    up = lambda n: -(-n // 256) * 256
+    B, Hq, Hkv, M, N = 2, 8, 2, 1000, 700
+    nqt, nkt = -(-M // 128), -(-N // 128)
+    npairs = -(-nqt // 2)
+    base = dict(batch=B, heads_q=Hq, heads_kv=Hkv, seqlen_q=M, seqlen_k=N, head_dim=128, value_dim=128,
+                causal=1, bias_kind=odf_b200.ODF_BIAS_ALIBI)
+    want = 256 + up(B * Hq * nqt * 4) + up(B * Hkv * nkt * 4) + up(B * Hq * npairs * 4)
+    assert lib.odf_fwd_workspace_size(C.byref(_params(**base))) == want
+    assert lib.odf_fwd_workspace_size(C.byref(_params(**dict(base, causal=0)))) == 256
+    assert lib.odf_fwd_workspace_size(C.byref(_params(**dict(base, head_dim=64, value_dim=64)))) == 256
+    assert lib.odf_fwd_workspace_size(C.byref(_params(**dict(base, bias_kind=0)))) == 256
+
+
 def test_misaligned_device_pointer_rejected():
     lib = odf_b200.load_library()
     assert lib.odf_flash_fwd_sm100(C.byref(_params(q=4096 + 2)), None) == odf_b200.ODF_ERR_INVALID_ARG

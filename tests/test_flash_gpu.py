@@ -213,6 +213,49 @@ def test_causal_alibi_far_tiles_diagonal_first(m, n, softcap):
     check_close(o, lse, o_ref, lse_ref, f"far tiles m={m} n={n} softcap={softcap}")
 
 
+@pytest.mark.parametrize("softcap,in_scale", [(0.0, 1.0), (50.0, 0.5)])
+def test_causal_alibi_norm_bound_leaves_out_only_far_tiles(softcap, in_scale):
+    """Causal ALiBi at d = 128 with a workspace: KV tiles that a Cauchy-Schwarz bound on the
+    tile norms shows to be far (every score below the row max by more than 48 ln 2) are not
+    visited at all.  Every tile left out must be far in float64 on the actual scores; a zero
+    slope leaves out nothing; steep slopes leave out most tiles; O and LSE match the oracle."""
+    torch = _torch()
+    import odf_b200
+    import oracle
+
+    H, M = 3, 1024
+    slopes = np.array([2.0, 0.25, 0.0], dtype=np.float32)
+    q, k, v = make_qkv(71, 1, H, H, M, M, 128, scale=in_scale)
+    nt = M // 128
+    visits = torch.zeros((H, nt, nt), dtype=torch.uint8, device="cuda")
+    o, lse = odf_b200.flash_fwd(to_dev(q), to_dev(k), to_dev(v), causal=True, alibi=True, alibi_slopes=slopes,
+                                softcap=softcap, visits=visits)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, alibi_slopes=slopes, softcap=softcap)
+    check_close(o.float().cpu().numpy(), lse.cpu().numpy(), o_ref, lse_ref, f"norm bound softcap={softcap}")
+
+    causal_map = oracle.tile_map(M, M, 128, 128, True, None, (128, 128)) != 0
+    processed = visits.cpu().numpy() != 0
+    assert np.array_equal(processed[2], causal_map), "zero slope: a tile was left out"
+    # slope 2: a KV tile two or more below a pair's first query tile is 258+ keys away (a bound
+    # of -500 against a margin of about 70), so each pair keeps only its band of three tiles
+    for qt in range(2, nt):
+        assert not processed[0, qt, :2 * (qt // 2) - 1].any(), f"steep slope: query tile {qt} visited a far tile"
+    scale = 1.0 / math.sqrt(128)
+    ii, jj = np.meshgrid(np.arange(M), np.arange(M), indexing="ij")
+    for h in range(H):
+        t = (q[0, h].astype(np.float64) @ k[0, h].astype(np.float64).T) * scale + float(slopes[h]) * (jj - ii)
+        if softcap > 0.0:
+            t = softcap * np.tanh(t / softcap)
+        t = np.where(jj <= ii, t, -np.inf)
+        row_max = t.max(axis=1, keepdims=True)
+        for qt in range(nt):
+            for kt in range(nt):
+                if causal_map[qt, kt] and not processed[h, qt, kt]:
+                    gap = (t[qt * 128:(qt + 1) * 128, kt * 128:(kt + 1) * 128] - row_max[qt * 128:(qt + 1) * 128]).max()
+                    assert gap < -48.0 * math.log(2.0), f"head {h} tile ({qt},{kt}) left out at gap {gap:.2f}"
+
+
 def test_explicit_alibi_slopes_and_noncausal_scale():
     H = 3
     slopes = np.array([0.5, 0.03125, 0.25], dtype=np.float32)
