@@ -65,12 +65,12 @@ constexpr int kWarpMma = 9;    // warps 10 and 11 only give their registers away
 // RegSplit::kSoftmax, which must not exceed what the block was launched with.  The host checks
 // the compiled register count before the first launch.
 constexpr int kLaunchRegs = 168;
-// The split is per score-mod variant: the variants with the larger control code (both score
-// mods, or the bias tensor) need 112 registers there, the others keep 200 for the softmax.
+// The split is per score-mod variant: the bias-tensor variants, with the larger control code,
+// need 112 registers there; the others keep 200 for the softmax.
 template <int MOD>
 struct RegSplit {
-    static constexpr int kCtrl = ((MOD & 7) == 3 || (MOD & 7) >= 4) ? 112 : 104;
-    static constexpr int kSoftmax = ((MOD & 7) == 3 || (MOD & 7) >= 4) ? 192 : 200;
+    static constexpr int kCtrl = (MOD & 7) >= 4 ? 112 : 104;
+    static constexpr int kSoftmax = (MOD & 7) >= 4 ? 192 : 200;
     static_assert(128 * kCtrl + 256 * kSoftmax <= kThreads * kLaunchRegs, "register split exceeds the launch");
     static_assert(kCtrl % 8 == 0 && kSoftmax % 8 == 0 && kSoftmax <= 256, "setmaxnreg operands");
 };
@@ -323,9 +323,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int64_t n_items = static_cast<int64_t>(args.batch) * args.heads_q * args.n_pairs;
-    // Greedy item assignment is compiled into the plain d = 128 kernel only (the shapes whose
-    // K/V outgrows L2 and whose speed depends on it); the other variants keep the fixed order.
-    constexpr bool kDyn = ((MOD & 7) == 0 && D == 128);
+    // Greedy item assignment is compiled into the plain d = 128 kernel (the shapes whose K/V
+    // outgrows L2 and whose speed depends on it) and the ALiBi d = 128 kernels (whose items'
+    // lengths vary by head once far tiles are left out); the other variants keep the fixed order.
+    constexpr bool kDyn = D == 128 && ((MOD & 7) == 0 || (MOD & (kModAlibi | kModBias)) == kModAlibi);
     volatile int64_t* item_q = reinterpret_cast<volatile int64_t*>(smem + Cfg::kOffQueue);
 
     if (threadIdx.x == 0) {
@@ -1557,10 +1558,14 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
             !L.has_bias) {  // the instantiation with greedy assignment compiled in
             a.sched = static_cast<unsigned long long*>(L.workspace);
             a.units_per_block = static_cast<int32_t>(per_block);
-            if (cudaMemsetAsync(L.workspace, 0, sizeof(unsigned long long), stream) != cudaSuccess) {
-                *err = "clearing the work-item counter failed";
-                return ODF_ERR_CUDA;
-            }
+        } else if (a.kv_reverse && L.workspace != nullptr && L.workspace_bytes >= kSchedBytes) {
+            // causal ALiBi: greedy over one block (pair-major over all heads), so that CTAs whose
+            // items lost their far tiles take more items
+            a.sched = static_cast<unsigned long long*>(L.workspace);
+        }
+        if (a.sched != nullptr && cudaMemsetAsync(L.workspace, 0, sizeof(unsigned long long), stream) != cudaSuccess) {
+            *err = "clearing the work-item counter failed";
+            return ODF_ERR_CUDA;
         }
     }
     if (a.mode == kModeList) {
