@@ -1208,13 +1208,27 @@ __global__ void pair_list_kernel(int32_t m, int32_t n, int32_t n_pairs, int32_t 
     if (lane == 0) count[pair] = base;
 }
 
-// Largest row norm ||x_r||_2 of each 128-row tile of a bf16 [batch, heads, rows, 128] tensor
-// (element strides {b, h, t}, rows 16-byte aligned): one block of 128 threads per
-// (batch, head, tile), 16 lanes reading a row's 256 bytes.  Rows at or beyond `rows` count 0.
-__global__ void __launch_bounds__(128) tile_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t sb, int64_t sh,
-                                                        int64_t st, int32_t heads, int32_t rows, int32_t n_tiles,
-                                                        float* __restrict__ out) {
-    const int64_t idx = blockIdx.x;
+// One bf16 [batch, heads, rows, 128] tensor for tile_norm_kernel (element strides {b, h, t},
+// rows 16-byte aligned) and its output, one float per (batch, head, 128-row tile).
+struct NormSrc {
+    const __nv_bfloat16* x;
+    int64_t sb, sh, st;
+    int32_t heads, rows, n_tiles;
+    int64_t n_blocks;  // batch * heads * n_tiles
+    float* out;
+};
+
+// Largest row norm ||x_r||_2 of each 128-row tile of Q (the first blocks) and of K (the rest):
+// one block of 128 threads per (batch, head, tile), 16 lanes reading a row's 256 bytes.  Rows
+// at or beyond `rows` count 0.
+__global__ void __launch_bounds__(128) tile_norm_kernel(const NormSrc src0, const NormSrc src1) {
+    const bool first = blockIdx.x < src0.n_blocks;
+    const NormSrc& S = first ? src0 : src1;
+    const __nv_bfloat16* __restrict__ x = S.x;
+    const int64_t sb = S.sb, sh = S.sh, st = S.st;
+    const int32_t heads = S.heads, rows = S.rows, n_tiles = S.n_tiles;
+    float* __restrict__ out = S.out;
+    const int64_t idx = first ? static_cast<int64_t>(blockIdx.x) : static_cast<int64_t>(blockIdx.x) - src0.n_blocks;
     const int tile = static_cast<int>(idx % n_tiles);
     const int64_t bh = idx / n_tiles;
     const int64_t b = bh / heads;
@@ -1248,7 +1262,8 @@ __global__ void __launch_bounds__(128) tile_norm_kernel(const __nv_bfloat16* __r
         out[idx] = sqrtf(fmaxf(fmaxf(warp_best[0], warp_best[1]), fmaxf(warp_best[2], warp_best[3])));
 }
 
-// Far KV tiles of causal ALiBi, from norms alone: for row qi and key kj of KV tile kt,
+// Far KV tiles of causal ALiBi, from norms alone (one warp per (batch, q-head, pair), its lanes
+// testing 32 KV tiles at a time): for row qi and key kj of KV tile kt,
 // |s scale| <= |scale| |q_i| |k_j| (Cauchy-Schwarz) bounds the score from above by
 //   U = c Kmax(kt) + slope (kt*128 + 127 - q0),   c = |scale| Qmax(qt) (1 + 2^-7)
 // and every row's max from below by its diagonal key (kj = qi, ALiBi term 0), L = -c Kmax(qt).
@@ -1259,9 +1274,10 @@ __global__ void __launch_bounds__(128) tile_norm_kernel(const __nv_bfloat16* __r
 // or non-finite norms keeps every tile.
 __global__ void far_lo_kernel(const FwdArgs a, const float* __restrict__ qn, const float* __restrict__ kn,
                               int32_t* __restrict__ kv_lo) {
-    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t idx = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
     const int64_t n_bh = static_cast<int64_t>(a.batch) * a.heads_q;
-    if (idx >= n_bh * a.n_pairs) return;
+    if (idx >= n_bh * a.n_pairs) return;  // whole warps leave together
     const int64_t bh = idx / a.n_pairs;
     const int pair = static_cast<int>(idx - bh * a.n_pairs);
     const int b = static_cast<int>(bh / a.heads_q);
@@ -1280,15 +1296,25 @@ __global__ void far_lo_kernel(const FwdArgs a, const float* __restrict__ qn, con
         if (qe - 1 < a.n && slope > 0.0f && isfinite(slope) && isfinite(c)) {
             const float L = -c * kn_u[qt];
             const float fL = a.softcap > 0.0f ? a.softcap * tanhf(L / a.softcap) : L;
-            for (; lo_q < qt; ++lo_q) {
-                const float U = c * kn_u[lo_q] + slope * static_cast<float>(lo_q * kTileK + kTileK - 1 - q0);
-                const float fU = a.softcap > 0.0f ? a.softcap * tanhf(U / a.softcap) : U;
-                if (!(fU < fL - thr)) break;  // NaN keeps the tile
+            for (int kt0 = 0; kt0 < qt; kt0 += 32) {
+                const int kt = kt0 + lane;
+                bool far = false;
+                if (kt < qt) {
+                    const float U = c * kn_u[kt] + slope * static_cast<float>(kt * kTileK + kTileK - 1 - q0);
+                    const float fU = a.softcap > 0.0f ? a.softcap * tanhf(U / a.softcap) : U;
+                    far = fU < fL - thr;  // NaN keeps the tile
+                }
+                const unsigned near = ~__ballot_sync(0xffffffffu, far) & (qt - kt0 >= 32 ? 0xffffffffu : ((1u << (qt - kt0)) - 1u));
+                if (near != 0u) {  // the first tile from 0 that is not far ends the scan
+                    lo_q = kt0 + __ffs(near) - 1;
+                    break;
+                }
+                lo_q = min(qt, kt0 + 32);
             }
         }
         lo = min(lo, lo_q);
     }
-    kv_lo[idx] = lo;
+    if (lane == 0) kv_lo[idx] = lo;
 }
 
 __global__ void convert_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, int64_t n) {
@@ -1592,14 +1618,13 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
         float* qn = reinterpret_cast<float*>(ws);
         float* kn = reinterpret_cast<float*>(ws + ((nq * 4 + 255) & ~int64_t{255}));
         int32_t* lo = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(kn) + ((nk * 4 + 255) & ~int64_t{255}));
-        tile_norm_kernel<<<static_cast<unsigned>(nq), 128, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(L.q), L.q_strides[0], L.q_strides[1], L.q_strides[2], a.heads_q, a.m,
-            a.n_qt, qn);
-        tile_norm_kernel<<<static_cast<unsigned>(nk), 128, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(L.k), L.k_strides[0], L.k_strides[1], L.k_strides[2], a.heads_kv, a.n,
-            a.n_kt, kn);
-        const int64_t n_lo = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;
-        far_lo_kernel<<<static_cast<unsigned>((n_lo + 127) / 128), 128, 0, stream>>>(a, qn, kn, lo);
+        const NormSrc sq{static_cast<const __nv_bfloat16*>(L.q), L.q_strides[0], L.q_strides[1], L.q_strides[2],
+                         a.heads_q, a.m, a.n_qt, nq, qn};
+        const NormSrc sk{static_cast<const __nv_bfloat16*>(L.k), L.k_strides[0], L.k_strides[1], L.k_strides[2],
+                         a.heads_kv, a.n, a.n_kt, nk, kn};
+        tile_norm_kernel<<<static_cast<unsigned>(nq + nk), 128, 0, stream>>>(sq, sk);
+        const int64_t n_lo = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;  // one warp each
+        far_lo_kernel<<<static_cast<unsigned>((n_lo + 3) / 4), 128, 0, stream>>>(a, qn, kn, lo);
         if (cudaGetLastError() != cudaSuccess) {
             *err = "far-tile bound kernel launch failed";
             return ODF_ERR_CUDA;
