@@ -1235,20 +1235,24 @@ __global__ void __launch_bounds__(128) tile_norm_kernel(const NormSrc src0, cons
     const int64_t h = bh - b * heads;
     const __nv_bfloat16* base = x + b * sb + h * sh;
     const int sub = threadIdx.x & 15;
-    float best = 0.0f;
-#pragma unroll 4
-    for (int r = threadIdx.x >> 4; r < kTileQ; r += 8) {
-        const int row = tile * kTileQ + r;
-        float ss = 0.0f;
-        if (row < rows) {
-            const uint4 u = __ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(row) * st) + sub);
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    // all 16 of the thread's loads are issued before any is used (256 bytes in flight per thread)
+    uint4 u[kTileQ / 8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float lo = __uint_as_float(w[i] << 16);
-                const float hi = __uint_as_float(w[i] & 0xFFFF0000u);
-                ss = fmaf(lo, lo, fmaf(hi, hi, ss));
-            }
+    for (int i = 0; i < kTileQ / 8; ++i) {
+        const int row = tile * kTileQ + (threadIdx.x >> 4) + 8 * i;
+        u[i] = row < rows ? __ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(row) * st) + sub)
+                          : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float best = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kTileQ / 8; ++i) {
+        const uint32_t w[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+        float ss = 0.0f;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float lo = __uint_as_float(w[t] << 16);
+            const float hi = __uint_as_float(w[t] & 0xFFFF0000u);
+            ss = fmaf(lo, lo, fmaf(hi, hi, ss));
         }
 #pragma unroll
         for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
