@@ -122,16 +122,18 @@ size_t odf_fwd_workspace_size(const odf_fwd_params* p);
  *
  * Instead of a caller workspace, a fixed array of ODF_NOALLOC_SCRATCH_BYTES in
  * this library's device memory (held by every GPU that loads the library until
- * the process exits) holds the work-item counter (256 bytes) and the block-mask
- * tile lists.  Limit: the lists take about ceil(seqlen_q/256) *
+ * the process exits) holds the work-item counter (256 bytes), the block-mask
+ * tile lists and, when it fits, causal ALiBi's far-tile bound (left out
+ * otherwise).  Limit: the lists take about ceil(seqlen_q/256) *
  * ceil(seqlen_k/128) * 4 bytes; larger problems are rejected with
  * ODF_ERR_UNSUPPORTED.  The first call on a device looks up the array's device
  * address (a one-time, non-allocating runtime call, repeated only if the
  * device's CUDA context changes); make that first call before any stream
  * capture.  All calls share the one array, which keeps what the last call left
  * there.  A launch that hands out work through the counter (long plain d = 128
- * problems) clears it first, and a block-mask launch rewrites the lists before
- * reading them; the other launches read nothing from the array.  So nothing
+ * problems, causal ALiBi at d = 128) clears it first, a block-mask launch rewrites
+ * the lists and a causal ALiBi launch the bound before reading them; the other
+ * launches read nothing from the array.  So nothing
  * needs to start at zero, but calls that overlap on the GPU, on different
  * streams, race on the array: serialise them.
  * No counterpart in the reference (its workspace is always caller-owned).
