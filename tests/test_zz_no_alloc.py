@@ -35,7 +35,8 @@ def _lib():
     return lib
 
 
-def _run(entry, q, k, v, mask, mask_block, causal, use_workspace, want_counter=False):
+def _run(entry, q, k, v, mask, mask_block, causal, use_workspace, want_counter=False, alibi_slopes=None,
+         softcap=0.0):
     """One call of `entry` on NaN-filled O/LSE (rows a call leaves out stay NaN).  With
     want_counter, also returns the work-item counter the workspace entry left in its workspace
     (0 when the launch used the fixed order, which never touches it)."""
@@ -47,8 +48,8 @@ def _run(entry, q, k, v, mask, mask_block, causal, use_workspace, want_counter=F
     lse = torch.full((B, Hq, M), float("nan"), dtype=torch.float32, device="cuda")
     mask_t = torch.as_tensor(mask, dtype=torch.uint8).cuda().contiguous() if mask is not None else None
     p, keep = odf_b200.fill_params(q, k, v, o, lse, causal=causal, scale=1.0 / np.sqrt(D), block_mask=mask_t,
-                                   mask_block=mask_block, alibi=False, alibi_slopes_host=None, softcap=0.0,
-                                   workspace=None, visits=None)
+                                   mask_block=mask_block, alibi=alibi_slopes is not None,
+                                   alibi_slopes_host=alibi_slopes, softcap=softcap, workspace=None, visits=None)
     ws = None
     if use_workspace:
         nbytes = _lib().odf_fwd_workspace_size(C.byref(p))
@@ -128,6 +129,29 @@ def test_noalloc_greedy_counter_path_two_calls_vs_oracle():
         qs, ks, vs = (t[:, heads, :R].float().cpu().numpy() for t in (q, k, v))
         o_ref, lse_ref = oracle.flash_fwd(qs, ks, vs, causal=True)
         _compare(o[:, heads, :R], lse[:, heads, :R], o_ref, lse_ref)
+
+
+def test_noalloc_causal_alibi_far_bound_two_calls():
+    """Causal ALiBi at d = 128 keeps its far-tile bound (tile norms, per-pair first KV tiles) and
+    its greedy work-item counter in the scratch: two calls in a row on NaN-filled outputs, each
+    bit for bit the workspace entry (same bound, same per-item arithmetic), with steep and flat
+    slopes so that some pairs leave out far tiles and some none; soft-cap on the second call."""
+    import torch
+
+    lib = _lib()
+    B, H, N, D = 1, 4, 2048, 128
+    slopes = np.array([2.0, 0.5, 0.01, 0.0], dtype=np.float32)
+    for call in range(2):
+        g = torch.Generator(device="cuda").manual_seed(90 + call)
+        q, k, v = (torch.randn((B, H, N, D), generator=g, device="cuda").to(torch.bfloat16) for _ in range(3))
+        softcap = 30.0 if call else 0.0
+        o_ws, lse_ws, counter = _run(lib.odf_flash_fwd_sm100, q, k, v, None, (128, 128), True, use_workspace=True,
+                                     want_counter=True, alibi_slopes=slopes, softcap=softcap)
+        assert counter is not None and counter > B * H * (N // 256), f"counter {counter}: greedy order not used"
+        o, lse = _run(lib.odf_flash_fwd_sm100_noalloc, q, k, v, None, (128, 128), True, use_workspace=False,
+                      alibi_slopes=slopes, softcap=softcap)
+        assert np.isfinite(o).all() and np.isfinite(lse).all(), f"call {call}: rows left unwritten"
+        assert np.array_equal(o, o_ws) and np.array_equal(lse, lse_ws), f"call {call}: differs from workspace entry"
 
 
 def test_noalloc_rejects_lists_beyond_scratch():
