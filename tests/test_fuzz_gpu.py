@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 O_REL_L2 = 1e-2
 O_MAX_ABS = 2e-2
 LSE_MAX_ABS = 1e-3
-N_CASES = 40
+N_CASES = 120
 
 
 def _case(i):
