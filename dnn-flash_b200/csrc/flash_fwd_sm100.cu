@@ -201,8 +201,8 @@ __device__ __forceinline__ Item decode_item(const FwdArgs& a, int64_t k) {
         I.h = I.hk * static_cast<int>(gq) + static_cast<int>(j - (j / gq) * gq);
         I.bh = I.b * a.heads_q + I.h;
     }
-    I.q00 = I.pair * 2 * kTileQ;
-    I.q01 = I.q00 + kTileQ;
+    I.q00 = I.pair * (a.single_tile ? 1 : 2) * kTileQ;
+    I.q01 = a.single_tile ? a.m : I.q00 + kTileQ;  // at M: Q1 has no rows, its epilogue writes none
     I.valid1 = I.q01 < a.m;
     I.qend0 = min(a.m, I.q00 + kTileQ);
     I.qend1 = I.valid1 ? min(a.m, I.q01 + kTileQ) : I.qend0;
@@ -1560,7 +1560,16 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
     int rc = ensure_device_ready(device, err);
     if (rc != ODF_OK) return rc;
     a.status = device_status_ptr(device);
-    a.n_pairs = (a.n_qt + 1) / 2;
+    int sm_count = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_device_mutex);
+        sm_count = g_devices[device].sm_count;
+    }
+    // one query tile per item when even that leaves SMs idle (not for block-mask lists or the
+    // causal ALiBi bound, which are built per pair)
+    a.single_tile = a.mode != kModeList && !a.kv_reverse && a.n_qt > 1 &&
+                    static_cast<int64_t>(a.batch) * a.heads_q * a.n_qt <= sm_count;
+    a.n_pairs = a.single_tile ? a.n_qt : (a.n_qt + 1) / 2;
     if (a.wait_limit_ns == 0) a.wait_limit_ns = kDefaultWaitLimitNs;
 
     CUtensorMap tq, tk, tv;
@@ -1641,11 +1650,6 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
     if (mod == 0 && L.head_dim == 128 && a.mode != kModeList && a.n_kt >= 48) mod = kModSkipMax;
     // persistent grid: one CTA per SM (the kernel's shared memory allows one), at most one per item
     const int64_t n_items = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;
-    int sm_count = 0;
-    {
-        std::lock_guard<std::mutex> lock(g_device_mutex);
-        sm_count = g_devices[device].sm_count;
-    }
     const dim3 grid(static_cast<unsigned>(n_items < sm_count ? n_items : sm_count), 1, 1);
     cudaError_t e = (L.head_dim == 64) ? launch_d<64>(tq, tk, tv, a, mod, grid, stream)
                                        : launch_d<128>(tq, tk, tv, a, mod, grid, stream);

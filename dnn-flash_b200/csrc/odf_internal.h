@@ -35,6 +35,9 @@ struct FwdArgs {
     int32_t o_bf16;
     int32_t batch, heads_q, heads_kv, m, n;
     int32_t n_qt, n_kt, n_pairs;
+    // Few-item problems (every query tile fits on its own SM): an item is one query tile (its Q1
+    // half left empty) instead of a pair, so twice as many SMs share the work.
+    int32_t single_tile;
     int32_t mode;
     int32_t causal;
     // Causal mode only: an item walks its KV tiles from the diagonal down to tile 0 (set for
