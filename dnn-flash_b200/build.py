@@ -16,6 +16,9 @@ PACKAGE_DIR = Path(__file__).resolve().parent
 ROOT = PACKAGE_DIR.parent
 CSRC = PACKAGE_DIR / "csrc"
 LIB = PACKAGE_DIR / "lib" / "libodf_sm100.so"
+# The same sources with the in-kernel invariant checks compiled in (-DODF_CHECKED): test
+# infrastructure (tests/test_checked_build_gpu.py), never loaded by the package itself.
+CHECKED_LIB = PACKAGE_DIR / "lib" / "libodf_sm100_checked.so"
 SOURCES = [CSRC / "flash_fwd_sm100.cu", CSRC / "odf_capi.cu"]
 CXX_API_SOURCES = [CSRC / "onednn_flash_api.cpp", CSRC / "planner.cpp"]
 DEPS = SOURCES + CXX_API_SOURCES + [CSRC / "sm100_ptx.cuh", CSRC / "softmax_math.cuh", CSRC / "odf_internal.h"] + sorted(
@@ -37,24 +40,26 @@ def nvcc() -> str:
     return cand if Path(cand).exists() else "nvcc"
 
 
-def up_to_date() -> bool:
-    if not LIB.exists():
+def up_to_date(lib: Path = LIB) -> bool:
+    if not lib.exists():
         return False
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     return all(p.stat().st_mtime <= t for p in DEPS if p.exists())
 
 
-def build_library(force: bool = False, verbose: bool = False) -> Path:
-    if not force and up_to_date():
-        return LIB
-    LIB.parent.mkdir(parents=True, exist_ok=True)
+def build_library(force: bool = False, verbose: bool = False, checked: bool = False) -> Path:
+    lib = CHECKED_LIB if checked else LIB
+    if not force and up_to_date(lib):
+        return lib
+    lib.parent.mkdir(parents=True, exist_ok=True)
     srcs = [str(s) for s in SOURCES + CXX_API_SOURCES if s.exists()]
-    cmd = [nvcc(), *NVCC_FLAGS, f"-I{ROOT / 'include'}", f"-I{CSRC}", "-shared", "-o", str(LIB) + ".tmp", *srcs]
+    cmd = [nvcc(), *NVCC_FLAGS, *(["-DODF_CHECKED"] if checked else []), f"-I{ROOT / 'include'}", f"-I{CSRC}",
+           "-shared", "-o", str(lib) + ".tmp", *srcs]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
-    os.replace(str(LIB) + ".tmp", LIB)
-    return LIB
+    os.replace(str(lib) + ".tmp", lib)
+    return lib
 
 
 def build_math_check(force: bool = False, verbose: bool = False) -> Path:
@@ -74,5 +79,6 @@ def build_math_check(force: bool = False, verbose: bool = False) -> Path:
 
 if __name__ == "__main__":
     build_library(force="--force" in sys.argv, verbose=True)
+    build_library(force="--force" in sys.argv, verbose=True, checked=True)
     build_math_check(force="--force" in sys.argv, verbose=True)
     print(LIB)

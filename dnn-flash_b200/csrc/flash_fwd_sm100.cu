@@ -87,6 +87,37 @@ constexpr float kRescaleLog2 = 8.0f;
 // n keys, far below fp32 resolution: its P is written as zeros without the exponentials.
 constexpr float kFarLog2 = 48.0f;
 
+// Checked build (compiled with -DODF_CHECKED; test infrastructure, never the shipped library):
+// in-kernel invariants whose failure sets a bit in g_check_bits and, if the status word is clean,
+// ODF_ERR_DEVICE_CHECK in it.  A failed check only records (it neither traps nor stops the
+// kernel); the accesses it describes stay inside their buffers either way (TMA zero-fills rows past
+// a tensor's end, and the epilogue writes no row at or past M).
+//   bit 0  a work item decodes to a pair, (batch, head), kv-head and entry count inside the problem
+//   bit 1  a KV entry names a tile inside K/V, needed by a query tile that has rows
+//   bit 2  the tensor-memory allocation starts at lane 0, column 0
+//   bit 3  the MMA warp waited for every ring load the producer issued, and for no other
+//   bit 4  per query tile, the MMA warp's P.V count equals the tiles the softmax warps finished
+//   bit 5  the causal ALiBi bound leaves each pair at least its diagonal tile
+#ifdef ODF_CHECKED
+__device__ unsigned int g_check_bits;
+__device__ __noinline__ void check_failed(int bit, int* status) {
+    atomicOr(&g_check_bits, 1u << bit);
+    if (status) atomicCAS(status, 0, ODF_ERR_DEVICE_CHECK);
+}
+#define ODF_CHECK(cond, bit)                                        \
+    do {                                                            \
+        if (!(cond)) check_failed((bit), args.status);              \
+    } while (0)
+#define ODF_COUNT(x) (++(x))
+#else
+#define ODF_CHECK(cond, bit) \
+    do {                     \
+    } while (0)
+#define ODF_COUNT(x) \
+    do {             \
+    } while (0)
+#endif
+
 // Score-mod variants: ALiBi and the same-shape bias are exclusive (one BiasKind per call).
 // kModSkipMax marks the plain-score variant for long KV ranges whose unmasked tiles skip the
 // row-max pass (the low three bits select the score mods).
@@ -361,6 +392,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+#ifdef ODF_CHECKED
+    // ring loads issued / waited for, P.V count of Q0 and Q1, tiles finished by Q0's and Q1's softmax
+    __shared__ int chk_counts[6];
+    if (threadIdx.x == 0) ODF_CHECK(tmem == 0u, 2);
+#endif
 
     if (warp >= kWarpProducer) {
         // Warpgroup 2 (producer, MMA issuer, two idle warps) hands registers to the
@@ -393,6 +429,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (k < 0) break;
                     const Item I = decode_item(args, k);
+                    ODF_CHECK(I.pair >= 0 && I.pair < args.n_pairs && I.bh >= 0 &&
+                                  I.bh < args.batch * args.heads_q && I.hk >= 0 && I.hk < args.heads_kv &&
+                                  I.n_entries >= 0 && I.n_entries <= args.n_kt,
+                              0);
+                    ODF_CHECK(args.kv_lo == nullptr || I.n_entries >= 1, 5);
                     if (I.n_entries == 0) continue;
                     // Q of this item replaces the previous item's once its last S MMAs have read it.
                     if (q_loads > 0 && !(ok = ptx::mbar_wait(bars.q_empty, (q_loads - 1) & 1, abort_flag, args.status,
@@ -411,6 +452,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ++q_loads;
                     for (int j = 0; ok && j < I.n_entries; ++j) {
                         const int kt = static_cast<int>(kv_entry(args, I, j) & 0xFFFFu);
+#ifdef ODF_CHECKED
+                        {
+                            const uint32_t e_chk = kv_entry(args, I, j);
+                            ODF_CHECK(kt < args.n_kt && kt * kTileK < args.n && (e_chk & (kNeed0 | kNeed1)) != 0 &&
+                                          (I.valid1 || !(e_chk & kNeed1)),
+                                      1);
+                        }
+#endif
                         for (int half = 0; half < 2; ++half) {
                             const int t = issued;
                             const int s = t % kSlots;
@@ -445,6 +494,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (q_loads > 0) ptx::mbar_wait(bars.q_full, (q_loads - 1) & 1, &no_abort, nullptr, 0, args.wait_limit_ns);
                 }
+#ifdef ODF_CHECKED
+                chk_counts[0] = issued;
+#endif
             }
         } else if (warp == kWarpMma) {
             // ------------------------------------------------------------ MMA issuer
@@ -462,6 +514,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bool acc[2] = {false, false};  // O_i already holds a P.V of the current item
                 int q_loads = 0;
                 bool ok = true;
+#ifdef ODF_CHECKED
+                int ring_waits = 0;
+#endif
 
                 // S_i = Q_i K^T (SS, M=128, N=128, K=D) into TMEM columns [128 i, 128 i + 128).
                 // Separate-P layout: S_i is overwritten once the softmax has read the previous one.
@@ -509,6 +564,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     return true;
                 };
                 auto wait_full = [&](int t) -> bool {
+#ifdef ODF_CHECKED
+                    ++ring_waits;
+#endif
                     return ptx::mbar_wait(&bars.slot_full[t % kSlots], (t / kSlots) & 1, abort_flag, args.status,
                                           ODF_ERR_DEVICE_TIMEOUT, args.wait_limit_ns);
                 };
@@ -610,6 +668,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::tc_commit(bars.drain);
                     ptx::mbar_wait(bars.drain, 0, &no_abort, nullptr, 0, args.wait_limit_ns);
                 }
+#ifdef ODF_CHECKED
+                chk_counts[1] = ring_waits;
+                chk_counts[2] = pv_count[0];
+                chk_counts[3] = pv_count[1];
+#endif
             }
         }
         // ------------------------------------------------------------ teardown (control side)
@@ -618,6 +681,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (warp == kWarpProducer) {
             ptx::tc_fence_after();
             ptx::tmem_dealloc(tmem, kTmemCols);
+#ifdef ODF_CHECKED
+            if (lane == 0 && !*abort_flag) {
+                ODF_CHECK(chk_counts[0] == chk_counts[1], 3);
+                ODF_CHECK(chk_counts[2] == chk_counts[4] && chk_counts[3] == chk_counts[5], 4);
+            }
+#endif
         }
     } else {
         // ------------------------------------------------------------ softmax warps
@@ -636,6 +705,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // bit 3: parity of the next pv_done wait, bit 4: a P_i was stored before (separate-P layout)
         uint32_t phases = 0;
         bool ok = true;
+#ifdef ODF_CHECKED
+        int tiles_done = 0;  // P_i handed to the MMA warp (p_full arrivals of this thread)
+#endif
 
         RowItem* rec_w = reinterpret_cast<RowItem*>(smem + Cfg::kOffRows) + warp;
         const volatile RowItem* rec = rec_w;
@@ -762,6 +834,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ptx::tmem_st_wait();
                             ptx::tc_fence_before();
                             ptx::mbar_arrive(&bars.p_full[qtile]);
+                            ODF_COUNT(tiles_done);
                             phases = (phases ^ 1u) | 4u;
                             if (row == 0 && args.visits) {
                                 args.visits[(static_cast<int64_t>(rec->bh) * args.n_qt + (q0 / kTileQ)) * args.n_kt +
@@ -883,6 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             store_zero_p(p_addr);
                             if (lane == 0) far_flags[qtile * 4 + wq] = 1;
                             ptx::mbar_arrive(&bars.p_full[qtile]);
+                            ODF_COUNT(tiles_done);
                             phases = (phases ^ 1u) | 4u;
                             continue;
                         }
@@ -971,6 +1045,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         store_zero_p(p_addr);
                         if (lane == 0) far_flags[qtile * 4 + wq] = 1;
                         ptx::mbar_arrive(&bars.p_full[qtile]);
+                        ODF_COUNT(tiles_done);
                         phases = (phases ^ 1u) | 4u;
                         continue;
                     }
@@ -1041,6 +1116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::tc_fence_before();
                 if (kFarSkip && lane == 0) far_flags[qtile * 4 + wq] = 0;
                 ptx::mbar_arrive(&bars.p_full[qtile]);
+                ODF_COUNT(tiles_done);
                 phases = (phases ^ 1u) | 4u;
             }
             if (!ok) break;
@@ -1131,6 +1207,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ teardown (softmax side)
         // Each role ends with its own copy of the CTA barrier, so the two register budgets
         // never meet in common code.
+#ifdef ODF_CHECKED
+        if (row == 0) chk_counts[4 + qtile] = tiles_done;
+#endif
         ptx::tc_fence_before();
         ptx::cta_barrier();
     }
@@ -1428,6 +1507,22 @@ size_t far_bound_bytes(int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t
     const int64_t n_kt = (seqlen_k + kTileK - 1) / kTileK;
     auto up = [](int64_t bytes) { return static_cast<size_t>((bytes + 255) & ~int64_t{255}); };
     return up(batch * heads_q * n_qt * 4) + up(batch * heads_kv * n_kt * 4) + up(batch * heads_q * n_pairs * 4);
+}
+
+int read_check_bits(uint32_t* out) {
+#ifdef ODF_CHECKED
+    unsigned int bits = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&bits, g_check_bits, sizeof(bits));
+    const unsigned int zero = 0;
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_check_bits, &zero, sizeof(zero));
+    if (e != cudaSuccess) return ODF_ERR_CUDA;
+    *out = bits;
+    return ODF_OK;
+#else
+    (void)out;
+    return ODF_ERR_UNSUPPORTED;
+#endif
 }
 
 void* current_context() {

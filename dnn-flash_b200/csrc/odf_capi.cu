@@ -594,6 +594,14 @@ int odf_device_status(int32_t* status_out, int32_t clear) {
 
 const char* odf_last_error(void) { return t_last_error.c_str(); }
 
+int odf_debug_check_bits(uint32_t* bits_out) {
+    if (bits_out == nullptr) return fail(ODF_ERR_INVALID_ARG, "bits_out must be non-null");
+    const int rc = odf::read_check_bits(bits_out);
+    if (rc == ODF_ERR_UNSUPPORTED) return fail(rc, "in-kernel checks exist only in the checked build");
+    if (rc != ODF_OK) return fail(rc, "reading the check bits failed");
+    return ODF_OK;
+}
+
 int odf_debug_set_wait(uint64_t limit_ns, int32_t stall_load) {
     if (limit_ns != 0 && (limit_ns < 1000000ull || limit_ns > 60000000000ull))
         return fail(ODF_ERR_INVALID_ARG, "wait limit must be 0 (default) or within [1 ms, 60 s]");

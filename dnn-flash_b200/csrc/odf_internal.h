@@ -110,6 +110,10 @@ int launch_convert_f32_bf16(const float* in, uint16_t* out, int64_t count, cudaS
 // current CUDA context changes (after cudaDeviceReset, or another context made current).
 int ensure_device_ready(int device, const char** err);
 
+// Checked build: the failed in-kernel invariant bits since the last call (read and cleared;
+// synchronises the device).  ODF_ERR_UNSUPPORTED in the shipped library.
+int read_check_bits(uint32_t* out);
+
 // The calling thread's current CUDA context (driver handle, NULL if none), fetched through the
 // runtime's driver entry point so the library needs no -lcuda.
 void* current_context();

@@ -38,6 +38,7 @@ extern "C" {
 #define ODF_ERR_CUDA 3             /* a CUDA runtime/driver call failed */
 #define ODF_ERR_DEVICE_TIMEOUT 4   /* a bounded in-kernel wait gave up (see odf_device_status) */
 #define ODF_ERR_NO_DEVICE 5        /* no sm_100 device current */
+#define ODF_ERR_DEVICE_CHECK 6     /* checked build only: an in-kernel invariant failed (odf_debug_check_bits) */
 
 /* Element types; values equal onednn_flash::DataType (score_mod_plan.hpp:7-11). */
 #define ODF_DTYPE_F32 0
@@ -183,6 +184,17 @@ int odf_device_status(int32_t* status_out, int32_t clear);
  * Failure drills and tests use it; a production caller never needs it.
  */
 int odf_debug_set_wait(uint64_t limit_ns, int32_t stall_load);
+
+/*
+ * Test hook of the checked build (the same sources compiled with -DODF_CHECKED into
+ * libodf_sm100_checked.so; no counterpart in the reference).  Synchronises the device, writes
+ * the in-kernel invariant bits that failed since the last call to *bits_out (0 = none) and
+ * clears them; a failure also sets ODF_ERR_DEVICE_CHECK in the status word if it was clean.
+ * Bits: 0 work-item decode, 1 KV entry, 2 tensor-memory base, 3 ring loads issued vs waited,
+ * 4 P.V count vs softmax tiles, 5 causal ALiBi bound.  The shipped library returns
+ * ODF_ERR_UNSUPPORTED.
+ */
+int odf_debug_check_bits(uint32_t* bits_out);
 
 /* Message for the last non-zero status returned on this host thread. */
 const char* odf_last_error(void);
