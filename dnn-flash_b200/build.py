@@ -64,12 +64,13 @@ def build_library(force: bool = False, verbose: bool = False, checked: bool = Fa
 
 def build_math_check(force: bool = False, verbose: bool = False) -> Path:
     """tests/cuda/lib/libodf_math_check.so (test infrastructure, not part of the library)."""
-    deps = [MATH_CHECK_SRC, CSRC / "softmax_math.cuh", CSRC / "sm100_ptx.cuh"]
+    deps = [MATH_CHECK_SRC, CSRC / "softmax_math.cuh", CSRC / "sm100_ptx.cuh", CSRC / "odf_internal.h"]
     if not force and MATH_CHECK_LIB.exists() and all(
             p.stat().st_mtime <= MATH_CHECK_LIB.stat().st_mtime for p in deps):
         return MATH_CHECK_LIB
     MATH_CHECK_LIB.parent.mkdir(parents=True, exist_ok=True)
-    cmd = [nvcc(), *NVCC_FLAGS, f"-I{CSRC}", "-shared", "-o", str(MATH_CHECK_LIB) + ".tmp", str(MATH_CHECK_SRC)]
+    cmd = [nvcc(), *NVCC_FLAGS, f"-I{ROOT / 'include'}", f"-I{CSRC}", "-shared", "-o", str(MATH_CHECK_LIB) + ".tmp",
+           str(MATH_CHECK_SRC)]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

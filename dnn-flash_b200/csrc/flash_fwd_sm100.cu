@@ -209,7 +209,33 @@ __device__ __forceinline__ Item decode_item(const FwdArgs& a, int64_t k) {
     Item I;
     const int64_t n_bh = static_cast<int64_t>(a.batch) * a.heads_q;
     const int64_t n_units = static_cast<int64_t>(a.batch) * a.heads_kv;
-    if (a.units_per_block >= n_units) {  // one block: pair-major over all heads
+    if (a.fast_decode) {  // the same decode in 32-bit arithmetic with the launch's dividers
+        const uint32_t x = static_cast<uint32_t>(k);
+        if (a.units_per_block >= n_units) {
+            const uint32_t round = fast_div(x, a.fd_bh);
+            I.bh = static_cast<int>(x - round * a.fd_bh.d);
+            I.pair = a.n_pairs - 1 - static_cast<int>(round);
+            I.b = static_cast<int>(fast_div(static_cast<uint32_t>(I.bh), a.fd_hq));
+            I.h = I.bh - I.b * a.heads_q;
+            I.hk = static_cast<int>(fast_div(static_cast<uint32_t>(I.h), a.fd_gq));
+        } else {
+            const uint32_t gq = a.fd_gq.d;
+            const uint32_t blk = fast_div(x, a.fd_block);
+            const uint32_t u0 = blk * static_cast<uint32_t>(a.units_per_block);
+            const uint32_t i = x - blk * a.fd_block.d;
+            const bool part = static_cast<int64_t>(u0) + a.units_per_block > n_units;  // the last, partial block
+            const FastDiv& fr = part ? a.fd_row_last : a.fd_row;                   // items per pair
+            const uint32_t pr = fast_div(i, fr);
+            const uint32_t j = i - pr * fr.d;
+            const uint32_t jq = fast_div(j, a.fd_gq);
+            const uint32_t unit = u0 + jq;
+            I.pair = a.n_pairs - 1 - static_cast<int>(pr);
+            I.b = static_cast<int>(fast_div(unit, a.fd_hkv));
+            I.hk = static_cast<int>(unit - static_cast<uint32_t>(I.b) * static_cast<uint32_t>(a.heads_kv));
+            I.h = I.hk * static_cast<int>(gq) + static_cast<int>(j - jq * gq);
+            I.bh = I.b * a.heads_q + I.h;
+        }
+    } else if (a.units_per_block >= n_units) {  // one block: pair-major over all heads
         const int64_t round = k / n_bh;
         I.bh = static_cast<int>(k - round * n_bh);
         I.pair = a.n_pairs - 1 - static_cast<int>(round);
@@ -1715,6 +1741,23 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
         }
         a.tile_list = list;
         a.tile_count = count;
+    }
+    // 32-bit item decode when every item index (and so every quantity the decode forms) fits
+    {
+        const int64_t items = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;
+        a.fast_decode = items <= INT32_MAX ? 1 : 0;
+        if (a.fast_decode) {
+            const uint32_t gq = static_cast<uint32_t>(a.heads_q / a.heads_kv);
+            const uint32_t upb = static_cast<uint32_t>(a.units_per_block);
+            const uint32_t last = static_cast<uint32_t>(n_units - (n_units - 1) / upb * upb);  // units of the last block
+            a.fd_bh = make_fastdiv(static_cast<uint32_t>(a.batch) * static_cast<uint32_t>(a.heads_q));
+            a.fd_hq = make_fastdiv(static_cast<uint32_t>(a.heads_q));
+            a.fd_gq = make_fastdiv(gq);
+            a.fd_hkv = make_fastdiv(static_cast<uint32_t>(a.heads_kv));
+            a.fd_block = make_fastdiv(upb * gq * static_cast<uint32_t>(a.n_pairs));
+            a.fd_row = make_fastdiv(upb * gq);
+            a.fd_row_last = make_fastdiv((last < upb ? last : upb) * gq);
+        }
     }
     // causal ALiBi: the norm bound over whole KV tiles, when the workspace has room for it
     a.kv_lo = nullptr;

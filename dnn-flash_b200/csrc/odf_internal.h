@@ -27,6 +27,36 @@ constexpr uint32_t kNeed1 = 1u << 17;
 constexpr uint32_t kBitmap0 = 1u << 18;
 constexpr uint32_t kBitmap1 = 1u << 19;
 
+// Division of 32-bit values by a divisor fixed for a launch, as one multiply-high, a subtract, an
+// add and two shifts (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, the round-up method of their section 4): with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1, every 32-bit x gives x / d = (t + ((x - t) >> 1)) >> (l - 1),
+// t = mulhi(x, m).  d = 1 takes m = 0 and shifts of 0.  The kernels decode a work item with these
+// instead of 64-bit divisions, which cost several hundred cycles each on the roles' critical paths.
+struct FastDiv {
+    uint32_t d, m, sh1, sh2;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f{d, 0u, 0u, 0u};
+    if (d <= 1) return f;
+    uint32_t l = 0;
+    while ((uint64_t{1} << l) < d) ++l;
+    f.m = static_cast<uint32_t>(((uint64_t{1} << 32) * ((uint64_t{1} << l) - d)) / d + 1);
+    f.sh1 = 1;
+    f.sh2 = l - 1;
+    return f;
+}
+
+__host__ __device__ __forceinline__ uint32_t fast_div(uint32_t x, const FastDiv& f) {
+#ifdef __CUDA_ARCH__
+    const uint32_t t = __umulhi(x, f.m);
+#else
+    const uint32_t t = static_cast<uint32_t>((static_cast<uint64_t>(x) * f.m) >> 32);
+#endif
+    return (t + ((x - t) >> f.sh1)) >> f.sh2;
+}
+
 // Everything the forward kernel needs besides the three tensor maps.
 struct FwdArgs {
     void* o;
@@ -66,6 +96,11 @@ struct FwdArgs {
     // every unit).
     unsigned long long* sched;
     int32_t units_per_block;
+    // Item decode in 32-bit arithmetic (set when every item index fits in 31 bits): dividers by
+    // batch * heads_q, heads_q, heads_q / heads_kv, heads_kv, the items of a full block of units,
+    // and the items per query-tile pair of a full and of the last (partial) block.
+    int32_t fast_decode;
+    FastDiv fd_bh, fd_hq, fd_gq, fd_hkv, fd_block, fd_row, fd_row_last;
     // Limit of every bounded in-kernel wait (ns); the host fills in the default of 2 s unless a
     // caller lowered it through odf_debug_set_wait.
     uint64_t wait_limit_ns;

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "odf_internal.h"
 #include "softmax_math.cuh"
 
 namespace {
@@ -33,9 +34,31 @@ __global__ void softcap_kernel(const float* __restrict__ s, float* __restrict__ 
     y[2 * i + 1] = odf::ptx::hi_f32(th) * softcap;
 }
 
+// q[i] = x[i] / d through the kernels' invariant-divisor division (odf::fast_div).
+__global__ void fastdiv_kernel(odf::FastDiv f, const uint32_t* __restrict__ x, uint32_t* __restrict__ q, int64_t n) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) q[i] = odf::fast_div(x[i], f);
+}
+
 }  // namespace
 
 extern "C" {
+
+// Host pointers; the host build of odf::make_fastdiv / odf::fast_div (no GPU needed).
+void odf_math_check_fastdiv_host(uint32_t d, const uint32_t* x, uint32_t* q, int64_t n) {
+    const odf::FastDiv f = odf::make_fastdiv(d);
+    for (int64_t i = 0; i < n; ++i) q[i] = odf::fast_div(x[i], f);
+}
+
+// Device pointers; the device build (multiply-high instruction), synchronous.
+int odf_math_check_fastdiv(uint32_t d, const uint32_t* x, uint32_t* q, int64_t n) {
+    if (n <= 0 || d == 0) return static_cast<int>(cudaErrorInvalidValue);
+    fastdiv_kernel<<<static_cast<unsigned>((n + 255) / 256), 256>>>(odf::make_fastdiv(d), x, q, n);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return static_cast<int>(e);
+}
+
 
 // Device pointers, n even; synchronous.  Returns a cudaError_t value (0 = success).
 int odf_math_check_exp2(const float* x, float* y_poly, float* y_mufu, int64_t n) {

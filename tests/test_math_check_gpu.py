@@ -36,6 +36,7 @@ def _lib():
     lib = C.CDLL(str(LIB))
     lib.odf_math_check_exp2.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64]
     lib.odf_math_check_softcap.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_float]
+    lib.odf_math_check_fastdiv.argtypes = [C.c_uint32, C.c_void_p, C.c_void_p, C.c_int64]
     return lib
 
 
@@ -89,3 +90,21 @@ def test_softcap_tanh_error_bound(softcap):
     assert err <= SOFTCAP_ABS_BOUND * softcap
     big = np.abs(exact) > 1e-5 * softcap
     assert np.all(np.sign(got[big]) == np.sign(exact[big]))
+
+
+def test_fastdiv_device_exact():
+    """The device build of the item decode's division (multiply-high instruction) equals x // d
+    for the divisors and dividends of tests/test_fastdiv.py."""
+    import torch
+
+    from test_fastdiv import DIVISORS, dividends
+
+    lib = _lib()
+    rng = np.random.default_rng(7)
+    for d in DIVISORS:
+        x = dividends(d, rng)
+        xd = torch.from_numpy(x.view(np.int32)).cuda()
+        qd = torch.empty_like(xd)
+        assert lib.odf_math_check_fastdiv(d, xd.data_ptr(), qd.data_ptr(), x.size) == 0
+        q = qd.cpu().numpy().view(np.uint32)
+        np.testing.assert_array_equal(q, (x.astype(np.uint64) // d).astype(np.uint32), err_msg=f"d={d}")
