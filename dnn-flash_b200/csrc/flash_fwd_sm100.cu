@@ -132,7 +132,7 @@ struct Config {
     static constexpr uint32_t kOffBar = kOffSlots + kSlots * kTileBytes;
     static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 2 + 2 + 2 * kItemQueue + 1;
     static constexpr uint32_t kOffRows = kOffBar + kNumBars * 8 + 16;  // after the barriers, TMEM slot, abort flag
-    static constexpr uint32_t kOffQueue = kOffRows + 8 * 40;             // item queue (int64 x kItemQueue)
+    static constexpr uint32_t kOffQueue = kOffRows + 8 * 48;             // item queue (int64 x kItemQueue)
     // same-shape bias: 2 KB per softmax warp to transpose coalesced row reads (32 rows x 16 keys)
     static constexpr uint32_t kOffBias = (kOffQueue + 8 * kItemQueue + 127) & ~127u;  // float4 stores
     static_assert(kOffBias % 16 == 0 && kOffRows % 8 == 0 && kOffQueue % 8 == 0, "shared-memory alignment");
@@ -172,16 +172,20 @@ struct RowItem {
     int bh, b, h;
     float slope;       // ALiBi slope of head h
     int64_t bias_off;  // same-shape bias: element offset of this (batch, head)'s plane
+    int kv0;           // first KV tile of the item's split of the key range
+    int split;         // which split (0 without KV splits)
 };
-static_assert(sizeof(RowItem) == 40, "RowItem layout");
+static_assert(sizeof(RowItem) == 48, "RowItem layout");
 
 // KV tile j of this query-tile pair: kv index in the low 16 bits, kNeed*/kBitmap* flags above.
-__device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, int pair, int j, bool valid1, int qend0, int qend1) {
+// With KV splits, entry j of an item is KV tile kv0 + j of its split (dense and causal modes).
+__device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, int pair, int j, bool valid1, int qend0, int qend1,
+                                             int kv0) {
     if (a.mode == kModeList) return __ldg(a.tile_list + static_cast<int64_t>(pair) * a.n_kt + j);
-    uint32_t e = static_cast<uint32_t>(j);
+    uint32_t e = static_cast<uint32_t>(kv0 + j);
     if (a.mode == kModeCausal) {
         // the pair's tiles 0 .. n_e - 1, in reverse with kv_reverse (diagonal first)
-        const int kt = a.kv_reverse ? min(a.n_kt, (qend1 + kTileK - 1) / kTileK) - 1 - j : j;
+        const int kt = a.kv_reverse ? min(a.n_kt, (qend1 + kTileK - 1) / kTileK) - 1 - j : kv0 + j;
         e = static_cast<uint32_t>(kt);
         if (kt * kTileK < qend0) e |= kNeed0;
         if (valid1 && kt * kTileK < qend1) e |= kNeed1;
@@ -199,14 +203,28 @@ struct Item {
     int qend0, qend1;  // their row ends (clipped to M)
     int n_entries;     // KV tiles visited by the pair (entries 0 .. n_entries - 1 of kv_entry)
     bool valid1;       // Q1 has rows
+    int split, kv0;    // KV split of the item and its first KV tile (0, 0 without splits)
 };
 
 // Items come in blocks of units_per_block (batch, kv-head) units: inside a block, item i is
 // query-tile pair n_pairs-1-i/(U G) (longest causal rows first) of q-head i mod (U G) of the
 // block (G = q-heads per kv-head).  A block's K/V fits in L2 while its CTAs stream through it.
-// With one block holding every unit this is plain pair-major order over all heads.
+// With one block holding every unit this is plain pair-major order over all heads.  With KV
+// splits, the n_splits splits of a pair's key range are consecutive items.
 __device__ __forceinline__ Item decode_item(const FwdArgs& a, int64_t k) {
     Item I;
+    I.split = 0;
+    if (a.n_splits > 1) {
+        if (a.fast_decode) {
+            const uint32_t q = fast_div(static_cast<uint32_t>(k), a.fd_split);
+            I.split = static_cast<int>(static_cast<uint32_t>(k) - q * a.fd_split.d);
+            k = q;
+        } else {
+            I.split = static_cast<int>(k % a.n_splits);
+            k /= a.n_splits;
+        }
+    }
+    I.kv0 = I.split * a.kv_per_split;
     const int64_t n_bh = static_cast<int64_t>(a.batch) * a.heads_q;
     const int64_t n_units = static_cast<int64_t>(a.batch) * a.heads_kv;
     if (a.fast_decode) {  // the same decode in 32-bit arithmetic with the launch's dividers
@@ -272,11 +290,12 @@ __device__ __forceinline__ Item decode_item(const FwdArgs& a, int64_t k) {
     } else {
         I.n_entries = a.n_kt;
     }
+    if (a.n_splits > 1) I.n_entries = max(0, min(a.kv_per_split, I.n_entries - I.kv0));  // this split's part
     return I;
 }
 
 __device__ __forceinline__ uint32_t kv_entry(const FwdArgs& a, const Item& I, int j) {
-    return kv_entry(a, I.pair, j, I.valid1, I.qend0, I.qend1);
+    return kv_entry(a, I.pair, j, I.valid1, I.qend0, I.qend1, I.kv0);
 }
 
 // Item assignment.  With a counter (args.sched) the producer warp of a CTA takes the next
@@ -379,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int64_t n_items = static_cast<int64_t>(args.batch) * args.heads_q * args.n_pairs;
+    const int64_t n_items = static_cast<int64_t>(args.batch) * args.heads_q * args.n_pairs * args.n_splits;
     // Greedy item assignment is compiled into the plain d = 128 kernel (the shapes whose K/V
     // outgrows L2 and whose speed depends on it) and the ALiBi d = 128 kernels (whose items'
     // lengths vary by head once far tiles are left out); the other variants keep the fixed order.
@@ -775,13 +794,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else if (!valid) {
                     r.n_iter = 0;
                 } else if (args.mode == kModeCausal && !args.kv_reverse) {  // tiles j with j * 128 < row end
-                    r.n_iter = min(I.n_entries, ((qtile == 0 ? I.qend0 : I.qend1) + kTileK - 1) / kTileK);
+                    r.n_iter = max(0, min(I.n_entries, ((qtile == 0 ? I.qend0 : I.qend1) + kTileK - 1) / kTileK - I.kv0));
                 } else {
                     r.n_iter = I.n_entries;
                 }
                 r.bh = I.bh;
                 r.b = I.b;
                 r.h = I.h;
+                r.kv0 = I.kv0;
+                r.split = I.split;
                 r.slope = 0.0f;
                 r.bias_off = (MOD & kModBias) ? static_cast<int64_t>(I.b) * args.bias_s0 +
                                                     static_cast<int64_t>(I.h) * args.bias_s1
@@ -800,7 +821,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             const int n_iter = rec->n_iter;
             for (int j = 0; j < n_iter; ++j) {
-                uint32_t e = static_cast<uint32_t>(j) | need_bit;
+                uint32_t e = static_cast<uint32_t>(rec->kv0 + j) | need_bit;
                 if (args.kv_reverse) {  // causal, diagonal first: entry j is tile n_entries - 1 - j
                     const int kt_r = rec->n_entries - 1 - j;
                     if (kt_r * kTileK >= min(args.m, rec->q0 + kTileQ)) continue;  // beyond this tile's rows
@@ -1168,7 +1189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // row, conflict-free both ways): a thread owning a row would write 32 rows x 16 B
                 // per store; read back, each store writes 8 rows x 64 contiguous bytes.
                 const int qw = rec->q0 + wq * 32;  // the warp's first row
-                const int64_t obase = static_cast<int64_t>(b) * args.o_stride_b +
+                const int64_t obase = static_cast<int64_t>(rec->split) * args.o_split +
+                                      static_cast<int64_t>(b) * args.o_stride_b +
                                       static_cast<int64_t>(h) * args.o_stride_h +
                                       static_cast<int64_t>(qw) * args.o_stride_t;
                 uint4* srow = reinterpret_cast<uint4*>(smem + Cfg::kOffBias) + warp * (32 * 4) + lane * 4;
@@ -1224,7 +1246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (valid_row && args.lse) {
                     const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-                    args.lse[static_cast<int64_t>(rec->bh) * args.m + qi] =
+                    args.lse[static_cast<int64_t>(rec->split) * args.lse_split + static_cast<int64_t>(rec->bh) * args.m + qi] =
                         (l_run > 0.0f) ? (m_use + log2f(l_run)) * kLn2 : -INFINITY;
                 }
             }
@@ -1515,7 +1537,106 @@ cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     return cudaGetLastError();
 }
 
+// Merge of the KV splits' partial results, one warp per (batch, q-head, query row): with the
+// splits' natural-log LSE_s and normalised O_s, LSE = log sum_s exp(LSE_s) and
+// O = sum_s exp(LSE_s - LSE) O_s (splits with LSE_s = -inf, no key of the row in them, weigh 0;
+// a row with no key at all gets O = 0 and LSE = -inf, as without splits).
+template <int D>
+__global__ void __launch_bounds__(256) split_combine_kernel(const float* __restrict__ po, const float* __restrict__ pl,
+                                                            int n_splits, int64_t o_split, int64_t l_split,
+                                                            int64_t rows, int m, int heads_q, void* o, int o_bf16,
+                                                            int64_t osb, int64_t osh, int64_t ost, float* lse) {
+    constexpr int V = D / 32;  // columns per lane
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;  // whole warps leave together
+    float mx = -INFINITY;
+    for (int sp = 0; sp < n_splits; ++sp) mx = fmaxf(mx, __ldg(pl + sp * l_split + row));
+    float acc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) acc[v] = 0.0f;
+    float sum = 0.0f;
+    if (mx != -INFINITY) {
+        for (int sp = 0; sp < n_splits; ++sp) {
+            const float l = __ldg(pl + sp * l_split + row);
+            if (l == -INFINITY) continue;
+            const float w = expf(l - mx);
+            sum += w;
+            const float* src = po + sp * o_split + row * D + lane * V;
+            if constexpr (V == 4) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(src));
+                acc[0] = fmaf(w, x.x, acc[0]);
+                acc[1] = fmaf(w, x.y, acc[1]);
+                acc[2] = fmaf(w, x.z, acc[2]);
+                acc[3] = fmaf(w, x.w, acc[3]);
+            } else {
+                const float2 x = __ldg(reinterpret_cast<const float2*>(src));
+                acc[0] = fmaf(w, x.x, acc[0]);
+                acc[1] = fmaf(w, x.y, acc[1]);
+            }
+        }
+    }
+    const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+    const int64_t bh = row / m;
+    const int64_t qi = row - bh * m;
+    const int64_t b = bh / heads_q;
+    const int64_t h = bh - b * heads_q;
+    const int64_t off = b * osb + h * osh + qi * ost + lane * V;
+    if (o_bf16) {
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(o) + off;
+        if constexpr (V == 4) {
+            *reinterpret_cast<uint2*>(dst) = make_uint2(ptx::pack_bf16x2(acc[0] * inv, acc[1] * inv),
+                                                        ptx::pack_bf16x2(acc[2] * inv, acc[3] * inv));
+        } else {
+            *reinterpret_cast<uint32_t*>(dst) = ptx::pack_bf16x2(acc[0] * inv, acc[1] * inv);
+        }
+    } else {
+        float* dst = static_cast<float*>(o) + off;
+        if constexpr (V == 4) {
+            *reinterpret_cast<float4*>(dst) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+        } else {
+            *reinterpret_cast<float2*>(dst) = make_float2(acc[0] * inv, acc[1] * inv);
+        }
+    }
+    if (lse != nullptr && lane == 0) lse[row] = mx == -INFINITY ? -INFINITY : mx + logf(sum);
+}
+
+// Bytes of the partial O (fp32) and LSE of `n_splits` KV splits, each plane 256-byte aligned.
+size_t split_partial_bytes(int64_t n_bh, int64_t m, int64_t d, int64_t n_splits) {
+    auto up = [](int64_t bytes) { return static_cast<size_t>((bytes + 255) & ~int64_t{255}); };
+    return up(n_splits * n_bh * m * d * 4) + up(n_splits * n_bh * m * 4);
+}
+
 }  // namespace
+
+SplitPlan plan_kv_splits(int64_t batch, int64_t heads_q, int64_t seqlen_q, int64_t seqlen_k, bool eligible,
+                         int64_t sm_count) {
+    const int64_t n_qt = (seqlen_q + kTileQ - 1) / kTileQ;
+    const int64_t n_kt = (seqlen_k + kTileK - 1) / kTileK;
+    SplitPlan sp{1, static_cast<int32_t>(n_kt)};
+    if (!eligible || n_kt < 2 || sm_count <= 0) return sp;
+    // the same item rule as the launch: single query tiles when each fits on its own SM
+    const bool single = n_qt > 1 && batch * heads_q * n_qt <= sm_count;
+    const int64_t items = batch * heads_q * (single ? n_qt : (n_qt + 1) / 2);
+    if (items <= 0 || 2 * items > sm_count) return sp;
+    // at least kMinSplitTiles KV tiles per split: an item's fixed costs (Q load, epilogue) and the
+    // merge launch outweigh fewer (c1, 4 KV tiles per query tile, measured 15.2 -> 18.0 us split in 4)
+    constexpr int64_t kMinSplitTiles = 4;
+    int64_t splits = sm_count / items < n_kt / kMinSplitTiles ? sm_count / items : n_kt / kMinSplitTiles;
+    if (splits < 2) return sp;
+    const int64_t per = (n_kt + splits - 1) / splits;
+    splits = (n_kt + per - 1) / per;
+    if (splits < 2) return sp;
+    sp.n_splits = static_cast<int32_t>(splits);
+    sp.kv_per_split = static_cast<int32_t>(per);
+    return sp;
+}
+
+size_t kv_split_bytes(int64_t batch, int64_t heads_q, int64_t seqlen_q, int64_t seqlen_k, int64_t head_dim,
+                      bool eligible) {
+    const SplitPlan sp = plan_kv_splits(batch, heads_q, seqlen_q, seqlen_k, eligible, kSplitSizingSms);
+    return sp.n_splits > 1 ? split_partial_bytes(batch * heads_q, seqlen_q, head_dim, sp.n_splits) : 0;
+}
 
 size_t workspace_bytes_for(int64_t seqlen_q, int64_t seqlen_k, bool has_mask) {
     if (!has_mask) return kSchedBytes;
@@ -1693,6 +1814,48 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
     a.n_pairs = a.single_tile ? a.n_qt : (a.n_qt + 1) / 2;
     if (a.wait_limit_ns == 0) a.wait_limit_ns = kDefaultWaitLimitNs;
 
+    // KV splits when the items leave SMs idle and the workspace has room for the partial results
+    // (as many splits as fit, down to none): O and LSE go to fp32 partials after the counter, and
+    // split_combine_kernel writes the caller's O and LSE after the forward kernel.
+    a.n_splits = 1;
+    a.kv_per_split = a.n_kt;
+    a.fd_split = make_fastdiv(1);
+    a.o_split = 0;
+    a.lse_split = 0;
+    void* const out_o = a.o;
+    float* const out_lse = a.lse;
+    const int32_t out_bf16 = a.o_bf16;
+    const int64_t out_sb = a.o_stride_b, out_sh = a.o_stride_h, out_st = a.o_stride_t;
+    const int64_t n_bh = static_cast<int64_t>(a.batch) * a.heads_q;
+    {
+        const bool eligible = L.allow_split && a.mode != kModeList && !a.kv_reverse && L.workspace != nullptr;
+        SplitPlan sp = plan_kv_splits(a.batch, a.heads_q, a.m, a.n, eligible, sm_count);
+        if (L.forced_splits > 0) sp.n_splits = eligible ? L.forced_splits : 1;
+        const size_t room = L.workspace_bytes > kSchedBytes ? L.workspace_bytes - kSchedBytes : 0;
+        int64_t splits = sp.n_splits;
+        while (splits > 1 && split_partial_bytes(n_bh, a.m, L.head_dim, splits) > room) --splits;
+        if (splits > 1) {
+            const int64_t per = (a.n_kt + splits - 1) / splits;
+            splits = (a.n_kt + per - 1) / per;
+        }
+        if (splits > 1) {
+            const int64_t per = (a.n_kt + splits - 1) / splits;
+            uint8_t* ws = static_cast<uint8_t*>(L.workspace) + kSchedBytes;
+            const int64_t o_plane = n_bh * a.m * L.head_dim;
+            a.n_splits = static_cast<int32_t>(splits);
+            a.kv_per_split = static_cast<int32_t>(per);
+            a.fd_split = make_fastdiv(static_cast<uint32_t>(splits));
+            a.o = ws;
+            a.o_bf16 = 0;
+            a.o_stride_b = static_cast<int64_t>(a.heads_q) * a.m * L.head_dim;
+            a.o_stride_h = static_cast<int64_t>(a.m) * L.head_dim;
+            a.o_stride_t = L.head_dim;
+            a.o_split = o_plane;
+            a.lse = reinterpret_cast<float*>(ws + ((splits * o_plane * 4 + 255) & ~int64_t{255}));
+            a.lse_split = n_bh * a.m;
+        }
+    }
+
     CUtensorMap tq, tk, tv;
     if (encode_bf16_4d(&tq, L.q, L.head_dim, a.m, a.heads_q, a.batch, L.q_strides) != CUDA_SUCCESS ||
         encode_bf16_4d(&tk, L.k, L.head_dim, a.n, a.heads_kv, a.batch, L.k_strides) != CUDA_SUCCESS ||
@@ -1713,12 +1876,12 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
         const int64_t kv_unit_bytes = 4 * static_cast<int64_t>(a.n) * L.head_dim;
         int64_t per_block = (int64_t{32} << 20) / (kv_unit_bytes > 0 ? kv_unit_bytes : 1);
         if (per_block < 1) per_block = 1;
-        if (per_block < n_units && a.mode != kModeList && L.workspace != nullptr &&
+        if (per_block < n_units && a.n_splits == 1 && a.mode != kModeList && L.workspace != nullptr &&
             L.workspace_bytes >= kSchedBytes && L.head_dim == 128 && !L.has_alibi && !L.has_softcap &&
             !L.has_bias) {  // the instantiation with greedy assignment compiled in
             a.sched = static_cast<unsigned long long*>(L.workspace);
             a.units_per_block = static_cast<int32_t>(per_block);
-        } else if (a.kv_reverse && L.workspace != nullptr && L.workspace_bytes >= kSchedBytes) {
+        } else if (a.kv_reverse && a.n_splits == 1 && L.workspace != nullptr && L.workspace_bytes >= kSchedBytes) {
             // causal ALiBi: greedy over one block (pair-major over all heads), so that CTAs whose
             // items lost their far tiles take more items
             a.sched = static_cast<unsigned long long*>(L.workspace);
@@ -1744,7 +1907,7 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
     }
     // 32-bit item decode when every item index (and so every quantity the decode forms) fits
     {
-        const int64_t items = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;
+        const int64_t items = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs * a.n_splits;
         a.fast_decode = items <= INT32_MAX ? 1 : 0;
         if (a.fast_decode) {
             const uint32_t gq = static_cast<uint32_t>(a.heads_q / a.heads_kv);
@@ -1787,10 +1950,25 @@ int launch_flash_fwd(FwdLaunch& L, cudaStream_t stream, const char** err) {
     // short or block-masked problems, with few unmasked tiles per row, it measured slower)
     if (mod == 0 && L.head_dim == 128 && a.mode != kModeList && a.n_kt >= 48) mod = kModSkipMax;
     // persistent grid: one CTA per SM (the kernel's shared memory allows one), at most one per item
-    const int64_t n_items = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs;
+    const int64_t n_items = static_cast<int64_t>(a.batch) * a.heads_q * a.n_pairs * a.n_splits;
     const dim3 grid(static_cast<unsigned>(n_items < sm_count ? n_items : sm_count), 1, 1);
     cudaError_t e = (L.head_dim == 64) ? launch_d<64>(tq, tk, tv, a, mod, grid, stream)
                                        : launch_d<128>(tq, tk, tv, a, mod, grid, stream);
+    if (e == cudaSuccess && a.n_splits > 1) {
+        const int64_t rows = n_bh * a.m;
+        const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+        const float* po = static_cast<const float*>(a.o);
+        if (L.head_dim == 64) {
+            split_combine_kernel<64><<<blocks, 256, 0, stream>>>(po, a.lse, a.n_splits, a.o_split, a.lse_split, rows, a.m,
+                                                                 a.heads_q, out_o, out_bf16, out_sb, out_sh, out_st,
+                                                                 out_lse);
+        } else {
+            split_combine_kernel<128><<<blocks, 256, 0, stream>>>(po, a.lse, a.n_splits, a.o_split, a.lse_split, rows,
+                                                                  a.m, a.heads_q, out_o, out_bf16, out_sb, out_sh,
+                                                                  out_st, out_lse);
+        }
+        e = cudaGetLastError();
+    }
     if (e != cudaSuccess) {
         *err = cudaGetErrorString(e);
         return ODF_ERR_CUDA;

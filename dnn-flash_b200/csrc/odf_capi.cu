@@ -130,12 +130,16 @@ int validate(const odf_fwd_params* p, bool host, Resolved* r) {
     return ODF_OK;
 }
 
-// Required workspace plus, for causal ALiBi at d = 128 (no block mask), the optional room for
-// its far-tile bound, for a launch of `batch` x `heads_q` query heads over `heads_kv` KV heads.
+// Required workspace plus the optional room of a launch of `batch` x `heads_q` query heads over
+// `heads_kv` KV heads: for causal ALiBi at d = 128 (no block mask) its far-tile bound; for other
+// launches without a block mask whose work items leave SMs idle, the partial results of KV splits.
 size_t workspace_with_far_bound(const odf_fwd_params* p, int64_t batch, int64_t heads_q, int64_t heads_kv) {
     size_t bytes = odf::workspace_bytes_for(p->seqlen_q, p->seqlen_k, p->block_mask != nullptr);
-    if (p->causal && p->block_mask == nullptr && p->bias_kind == ODF_BIAS_ALIBI && p->head_dim == 128)
+    const bool alibi_walk = p->causal && p->bias_kind == ODF_BIAS_ALIBI && p->head_dim == 128;
+    if (p->block_mask == nullptr && alibi_walk)
         bytes += odf::far_bound_bytes(batch, heads_q, heads_kv, p->seqlen_q, p->seqlen_k);
+    if (p->block_mask == nullptr && !alibi_walk)
+        bytes += odf::kv_split_bytes(batch, heads_q, p->seqlen_q, p->seqlen_k, p->head_dim, true);
     return bytes;
 }
 
@@ -158,6 +162,7 @@ odf::FwdLaunch make_launch(const odf_fwd_params* p, const Resolved& r) {
     L.has_bias = p->bias_kind == ODF_BIAS_SAME_SHAPE;
     L.workspace = p->workspace;
     L.workspace_bytes = p->workspace_bytes;
+    L.allow_split = 1;
     odf::FwdArgs& a = L.args;
     a.o = p->o;
     a.lse = p->lse;
@@ -210,7 +215,8 @@ odf::FwdLaunch make_launch(const odf_fwd_params* p, const Resolved& r) {
     return L;
 }
 
-int run_device(const odf_fwd_params* p, const Resolved& r, cudaStream_t stream) {
+int run_device(const odf_fwd_params* p, const Resolved& r, cudaStream_t stream, bool allow_split = true,
+               int forced_splits = 0) {
     const size_t need = odf::workspace_bytes_for(p->seqlen_q, p->seqlen_k, p->block_mask != nullptr);
     if (p->block_mask != nullptr && p->workspace == nullptr)
         return fail(ODF_ERR_INVALID_ARG, "a block mask needs a device workspace of odf_fwd_workspace_size() bytes");
@@ -219,6 +225,8 @@ int run_device(const odf_fwd_params* p, const Resolved& r, cudaStream_t stream) 
     if (p->workspace != nullptr && !aligned16(p->workspace))
         return fail(ODF_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
     odf::FwdLaunch L = make_launch(p, r);
+    L.allow_split = allow_split ? 1 : 0;
+    L.forced_splits = forced_splits;
     const char* err = "";
     const int rc = odf::launch_flash_fwd(L, stream, &err);
     if (rc != ODF_OK) return fail(rc, err);
@@ -409,6 +417,15 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
     }
     // a chunk launches batch 1 over at most all query heads and all units
     const size_t ws_bytes = workspace_with_far_bound(p, 1, p->batch * p->heads_q, units);
+    // Every chunk splits the key range as one device launch of the whole problem would, so each
+    // query tile is computed the same way (and the result equals odf_flash_fwd_sm100's bit for bit).
+    int sm_count = 0;
+    if ((e = cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+        return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
+    const bool alibi_walk = p->causal && p->bias_kind == ODF_BIAS_ALIBI && p->head_dim == 128;
+    const int whole_splits = odf::plan_kv_splits(p->batch, p->heads_q, p->seqlen_q, p->seqlen_k,
+                                                 p->block_mask == nullptr && !alibi_walk, sm_count)
+                                 .n_splits;
 
     for (int64_t c = 0; c < static_cast<int64_t>(plan.size()); ++c) {
         const int64_t u0 = plan[c].u0, cu = plan[c].cu, g0 = plan[c].g0, ng = plan[c].ng;
@@ -526,7 +543,7 @@ int odf_flash_fwd_host(const odf_fwd_params* p) {
         e = cudaStreamWaitEvent(s_comp, pool.in_done[slot], 0);
         if (e == cudaSuccess && c >= kHostSets) e = cudaStreamWaitEvent(s_comp, pool.out_done[slot], 0);
         if (e != cudaSuccess) return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
-        rc = run_device(&sub, rs, s_comp);
+        rc = run_device(&sub, rs, s_comp, true, whole_splits);
         if (rc != ODF_OK) return rc;
         if ((e = cudaEventRecord(pool.comp_done[slot], s_comp)) != cudaSuccess)
             return fail(ODF_ERR_CUDA, cudaGetErrorString(e));
@@ -679,5 +696,5 @@ extern "C" int odf_flash_fwd_sm100_noalloc(const odf_fwd_params* p, void* stream
         q.workspace = scratch;
         q.workspace_bytes = ODF_NOALLOC_SCRATCH_BYTES;
     }
-    return run_device(&q, r, static_cast<cudaStream_t>(stream));
+    return run_device(&q, r, static_cast<cudaStream_t>(stream), false);  // the scratch keeps its layout: no KV splits
 }

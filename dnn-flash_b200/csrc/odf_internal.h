@@ -101,6 +101,13 @@ struct FwdArgs {
     // and the items per query-tile pair of a full and of the last (partial) block.
     int32_t fast_decode;
     FastDiv fd_bh, fd_hq, fd_gq, fd_hkv, fd_block, fd_row, fd_row_last;
+    // KV splits (n_splits > 1; dense and causal modes without the ALiBi far-tile walk): every
+    // query-tile pair becomes n_splits items over consecutive kv_per_split KV tiles each, whose
+    // normalised O (fp32) and LSE go to per-split planes o_split / lse_split elements apart (o and
+    // lse then point at workspace partials), merged afterwards by split_combine_kernel.
+    int32_t n_splits, kv_per_split;
+    FastDiv fd_split;
+    int64_t o_split, lse_split;
     // Limit of every bounded in-kernel wait (ns); the host fills in the default of 2 s unless a
     // caller lowered it through odf_debug_set_wait.
     uint64_t wait_limit_ns;
@@ -128,6 +135,8 @@ struct FwdLaunch {
     FwdArgs args;
     void* workspace;
     size_t workspace_bytes;
+    int32_t allow_split;    // KV splits may use the workspace (0: the layout of a workspace without them)
+    int32_t forced_splits;  // > 0: this many KV splits (1: none) instead of the launch's own plan
 };
 
 // Launch the tile-list builder (block-mask mode) and the forward kernel on `stream`.
@@ -157,6 +166,22 @@ void* current_context();
 int* device_status_ptr(int device);
 
 size_t workspace_bytes_for(int64_t seqlen_q, int64_t seqlen_k, bool has_mask);
+
+// KV splits: when a launch's work items (query-tile pairs, or single query tiles) would leave more
+// than half of `sm_count` SMs idle, each item's key range is cut into n_splits consecutive parts of
+// kv_per_split (at least 4) KV tiles, one item each, and the parts are merged afterwards
+// (n_splits = 1: none).
+// Not for block-mask lists or the causal ALiBi walk at d = 128 (`eligible` false).
+struct SplitPlan {
+    int32_t n_splits, kv_per_split;
+};
+SplitPlan plan_kv_splits(int64_t batch, int64_t heads_q, int64_t seqlen_q, int64_t seqlen_k, bool eligible,
+                         int64_t sm_count);
+// Optional workspace bytes after kSchedBytes for the fp32 partial O and LSE of that plan (0 without
+// splits), sized for a GPU of kSplitSizingSms SMs.
+constexpr int64_t kSplitSizingSms = 148;
+size_t kv_split_bytes(int64_t batch, int64_t heads_q, int64_t seqlen_q, int64_t seqlen_k, int64_t head_dim,
+                      bool eligible);
 
 // Optional workspace bytes after workspace_bytes_for(..., false) that causal ALiBi at d = 128
 // uses for its far-tile bound (tile norms and the per-pair first visited KV tile).

@@ -114,6 +114,49 @@ def test_workspace_room_for_causal_alibi_far_bound():
     assert lib.odf_fwd_workspace_size(C.byref(_params(**dict(base, bias_kind=0)))) == 256
 
 
+def _split_plan(B, Hq, M, N, sms=148):
+    """The KV-split rule restated: (number of splits, KV tiles per split)."""
+    nqt, nkt = -(-M // 128), -(-N // 128)
+    single = nqt > 1 and B * Hq * nqt <= sms
+    items = B * Hq * (nqt if single else -(-nqt // 2))
+    s = min(sms // items, nkt // 4)  # at least four KV tiles per split
+    if s < 2 or 2 * items > sms:
+        return 1, nkt
+    per = -(-nkt // s)
+    return -(-nkt // per), per
+
+
+def test_workspace_room_for_kv_splits():
+    """Launches whose work items would leave more than half of a 148-SM GPU idle ask for optional
+    room after the 256-byte counter for the fp32 partial O [splits, B, Hq, M, Dv] and LSE
+    [splits, B, Hq, M] of their KV splits, each plane rounded up to 256 bytes.  Block masks, causal
+    ALiBi at d = 128 and shapes with enough items ask for none."""
+    lib = odf_b200.load_library()
+    up = lambda n: -(-n // 256) * 256
+    for B, Hq, Hkv, M, N, D, causal in [(1, 2, 1, 128, 4096, 128, 0), (1, 4, 4, 512, 2048, 64, 0),
+                                         (2, 1, 1, 300, 1900, 128, 1), (1, 3, 3, 1, 4096, 64, 0)]:
+        s, per = _split_plan(B, Hq, M, N)
+        assert s > 1
+        base = dict(batch=B, heads_q=Hq, heads_kv=Hkv, seqlen_q=M, seqlen_k=N, head_dim=D, value_dim=D,
+                    causal=causal)
+        want = 256 + up(s * B * Hq * M * D * 4) + up(s * B * Hq * M * 4)
+        assert lib.odf_fwd_workspace_size(C.byref(_params(**base))) == want, (B, Hq, M, N, D)
+    assert _split_plan(1, 4, 512, 512) == (1, 4)  # BASELINE c1: four KV tiles per query tile, too few to split
+    assert _split_plan(1, 2, 128, 4096) == (8, 4)
+    assert _split_plan(1, 8, 64, 32768) == (18, 15)
+    assert _split_plan(8, 16, 4096, 4096) == (1, 32)  # c4: enough items, no splits
+    # enough items, a block mask, or the causal ALiBi walk at d = 128: no split room
+    big = dict(batch=8, heads_q=16, heads_kv=16, seqlen_q=2048, seqlen_k=2048, head_dim=128, value_dim=128)
+    assert lib.odf_fwd_workspace_size(C.byref(_params(**big))) == 256
+    dec = dict(batch=1, heads_q=2, heads_kv=2, seqlen_q=128, seqlen_k=4096, head_dim=128, value_dim=128)
+    masked = _params(**dict(dec, block_mask=4096, mask_qbs=128, mask_kbs=128, mask_qblocks=1, mask_kblocks=32))
+    nolist = lib.odf_fwd_workspace_size(C.byref(masked))
+    assert nolist == 256 + up(1 * 32 * 4) + up(1 * 4)  # the tile lists alone
+    walk = _params(**dict(dec, causal=1, bias_kind=odf_b200.ODF_BIAS_ALIBI))
+    nqt, nkt = 1, 32
+    assert lib.odf_fwd_workspace_size(C.byref(walk)) == 256 + up(2 * nqt * 4) + up(2 * nkt * 4) + up(2 * 1 * 4)
+
+
 def test_misaligned_device_pointer_rejected():
     lib = odf_b200.load_library()
     assert lib.odf_flash_fwd_sm100(C.byref(_params(q=4096 + 2)), None) == odf_b200.ODF_ERR_INVALID_ARG

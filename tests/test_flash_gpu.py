@@ -757,3 +757,111 @@ def test_few_query_rows_long_keys(m, causal, want_lse):
     o_ref, lse_ref = oracle_fwd(q, k, v, causal=causal)
     assert (lse is None) == (not want_lse)
     check_close(o, lse, o_ref, lse_ref if want_lse else None, f"m={m} causal={causal}")
+
+
+# --------------------------------------------------------------------------- KV splits
+def _splits_of(q, k, v, **kw):
+    """Workspace bytes the launch asks for beyond the 256-byte counter (> 0: it splits its keys)."""
+    import ctypes as C
+
+    import odf_b200
+
+    torch = _torch()
+    qd, kd, vd = to_dev(q), to_dev(k), to_dev(v)
+    o = torch.empty(qd.shape[:3] + (vd.shape[3],), dtype=torch.float32, device="cuda")
+    lse = torch.empty(qd.shape[:3], dtype=torch.float32, device="cuda")
+    p, keep = odf_b200.fill_params(qd, kd, vd, o, lse, causal=kw.get("causal", False),
+                                   scale=1.0 / math.sqrt(q.shape[3]), block_mask=None, mask_block=(128, 128),
+                                   alibi=kw.get("alibi", False), alibi_slopes_host=None,
+                                   softcap=kw.get("softcap", 0.0), workspace=None, visits=None)
+    return odf_b200.load_library().odf_fwd_workspace_size(C.byref(p)) - 256
+
+
+def _run_without_workspace(q, k, v, **kw):
+    """The same launch through the C ABI without a workspace: no KV splits, fixed order."""
+    import ctypes as C
+
+    import odf_b200
+
+    torch = _torch()
+    qd, kd, vd = to_dev(q), to_dev(k), to_dev(v)
+    o = torch.empty(qd.shape[:3] + (vd.shape[3],), dtype=torch.float32, device="cuda")
+    lse = torch.empty(qd.shape[:3], dtype=torch.float32, device="cuda")
+    p, keep = odf_b200.fill_params(qd, kd, vd, o, lse, causal=kw.get("causal", False),
+                                   scale=1.0 / math.sqrt(q.shape[3]), block_mask=None, mask_block=(128, 128),
+                                   alibi=kw.get("alibi", False), alibi_slopes_host=None,
+                                   softcap=kw.get("softcap", 0.0), workspace=None, visits=None,
+                                   bias=kw.get("bias"))
+    lib = odf_b200.load_library()
+    assert lib.odf_flash_fwd_sm100(C.byref(p), C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0, \
+        odf_b200.last_error()
+    torch.cuda.synchronize()
+    return o.cpu().numpy(), lse.cpu().numpy()
+
+
+KV_SPLIT_CASES = {
+    # (B, Hq, Hkv, M, N, D, kwargs): few query tiles over long key ranges, the shapes whose items
+    # would leave most SMs idle without splits
+    "decode_dense_d128_ragged": (1, 2, 1, 64, 3000, 128, {}),
+    "decode_dense_d64": (1, 3, 3, 1, 4096, 64, {}),
+    "causal_d64_later_splits_empty": (1, 2, 2, 200, 2500, 64, {"causal": True}),
+    "causal_d128_square": (1, 1, 1, 1024, 1024, 128, {"causal": True}),
+    "gqa_dense_d128": (1, 4, 1, 128, 4096, 128, {}),
+    "alibi_softcap_dense_d128": (1, 3, 3, 130, 2100, 128, {"alibi": True, "softcap": 30.0}),
+    "alibi_causal_d64": (1, 2, 2, 256, 2048, 64, {"alibi": True, "causal": True}),
+    "softcap_causal_d128": (2, 1, 1, 300, 1900, 128, {"softcap": 15.0, "causal": True}),
+}
+
+
+@pytest.mark.parametrize("case", sorted(KV_SPLIT_CASES))
+def test_kv_splits_vs_oracle(case):
+    """Launches whose work items would leave more than half of the SMs idle cut each item's key
+    range into splits (one item each), write normalised fp32 partials and merge them by their LSE.
+    The merged O/LSE match the oracle, and the same launch without a workspace (no splits) agrees
+    within the same tolerances; rows with no key in a split (causal) weigh it 0."""
+    import oracle
+
+    B, Hq, Hkv, M, N, D, kw = KV_SPLIT_CASES[case]
+    q, k, v = make_qkv(40 + len(case), B, Hq, Hkv, M, N, D, scale=0.7)
+    assert _splits_of(q, k, v, **kw) > 0, "this shape should split its key range"
+    o, lse = run_gpu(q, k, v, **kw)
+    okw = {"causal": kw.get("causal", False), "softcap": kw.get("softcap", 0.0)}
+    if kw.get("alibi"):
+        okw["alibi_slopes"] = oracle.alibi_slopes(Hq)
+    o_ref, lse_ref = oracle_fwd(q, k, v, **okw)
+    check_close(o, lse, o_ref, lse_ref, f"kv splits {case}")
+    o_one, lse_one = _run_without_workspace(q, k, v, **kw)
+    check_close(o_one, lse_one, o_ref, lse_ref, f"no splits {case}")
+
+
+def test_kv_splits_same_shape_bias():
+    """A strided same-shape bias with KV splits (key offsets of later splits) against the oracle."""
+    B, H, M, N, D = 1, 2, 100, 1800, 128
+    q, k, v = make_qkv(47, B, H, H, M, N, D)
+    bias = _bias(11, (B, H, M, N))
+    assert _splits_of(q, k, v, causal=True) > 0
+    o, lse = run_gpu(q, k, v, causal=True, bias=to_dev(bias, _torch().float32))
+    o_ref, lse_ref = oracle_fwd(q, k, v, causal=True, bias=bias)
+    check_close(o, lse, o_ref, lse_ref, "kv splits bias")
+
+
+@pytest.mark.parametrize("in_dtype", ["f32", "bf16"])
+def test_kv_splits_host_entry_equals_device_entry(in_dtype):
+    """The host entry's chunks split the key range as one device launch of the whole problem does,
+    so the two results are equal bit for bit (and match the oracle)."""
+    import odf_b200
+
+    B, H, Hk, M, N, D = 1, 4, 2, 100, 3000, 128
+    q, k, v = make_qkv(48, B, H, Hk, M, N, D)
+    assert _splits_of(q, k, v) > 0
+    if in_dtype == "f32":
+        hq, hk, hv = q, k, v
+    else:
+        hq, hk, hv = (np.ascontiguousarray((x.view(np.uint32) >> 16).astype(np.uint16)) for x in (q, k, v))
+    lse = np.empty((B, H, M), dtype=np.float32)
+    o, _ = odf_b200.flash_fwd_host(hq, hk, hv, lse_out=lse)
+    o_dev, lse_dev = run_gpu(q, k, v)
+    assert np.array_equal(o, o_dev)
+    assert np.array_equal(lse, lse_dev)
+    o_ref, lse_ref = oracle_fwd(q, k, v)
+    check_close(o, lse, o_ref, lse_ref, "kv splits host entry")
