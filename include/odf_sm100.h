@@ -106,8 +106,11 @@ int odf_flash_fwd_sm100(const odf_fwd_params* p, void* stream);
 /* Device scratch bytes for these params: 256 (the work-item counter, optional) plus,
    with a block mask, the per-query-tile-pair KV lists (required), or, for causal ALiBi at
    head_dim 128, room for the far-tile bound (tile norms and per-pair first KV tiles;
-   optional: a smaller workspace runs without the bound).  Plays the role of
-   AttentionWorkspace::resize (src/onednn_flash/attention_workspace.cpp:5-20). */
+   optional: a smaller workspace runs without the bound), or, for other launches whose work
+   items would leave more than half of the GPU's SMs idle (few heads or query tiles over a
+   long key range), room for the fp32 partial O and LSE of KV splits (optional: a smaller
+   workspace splits less or not at all).  Plays the role of AttentionWorkspace::resize
+   (src/onednn_flash/attention_workspace.cpp:5-20). */
 size_t odf_fwd_workspace_size(const odf_fwd_params* p);
 
 /* Capacity of the library-owned scratch used by odf_flash_fwd_sm100_noalloc. */
