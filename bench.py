@@ -15,7 +15,7 @@ Ranks share nothing on the data path (heads are independent): the only
 collectives are the barrier and the max-over-ranks of the timed region.
 
 Usage:
-  python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--config c1..c5|mha8k_causal|mha8k_dense]
+  python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--config c1..c5|mha8k_causal|mha8k_dense|bias8k|bias8k_full|decode8k|decode32k_gqa]
   torchrun --nproc-per-node N bench.py --gpus N ...
 """
 from __future__ import annotations
@@ -61,6 +61,12 @@ CONFIGS = {
                    out="bf16", mask=None, bias="broadcast"),
     "bias8k_full": dict(B=1, Hq=16, Hkv=16, N=8192, D=128, causal=True, alibi=False, softcap=0.0, in_scale=1.0,
                         out="bf16", mask=None, bias="full"),
+    # Not BASELINE configs: few query rows (M) over a long key range (N), whose query-tile items
+    # would leave most SMs idle; the launch splits the key range (decode / chunked prefill).
+    "decode8k": dict(B=1, Hq=8, Hkv=8, M=128, N=8192, D=128, causal=False, alibi=False, softcap=0.0, in_scale=1.0,
+                     out="bf16", mask=None),
+    "decode32k_gqa": dict(B=1, Hq=8, Hkv=1, M=64, N=32768, D=128, causal=False, alibi=False, softcap=0.0,
+                          in_scale=1.0, out="bf16", mask=None),
 }
 WORKLOAD_NAMES = {
     "c1": "c1_mha_noncausal_b1h4_n512_d64",
@@ -72,6 +78,8 @@ WORKLOAD_NAMES = {
     "mha8k_dense": "mha_dense_b2h32_n8192_d128",
     "bias8k": "bias_broadcast_nxn_causal_b2h32_n8192_d128",
     "bias8k_full": "bias_full_bhnn_causal_b1h16_n8192_d128",
+    "decode8k": "decode_b1h8_m128_n8192_d128",
+    "decode32k_gqa": "decode_gqa_b1_hq8_hkv1_m64_n32768_d128",
 }
 
 
@@ -87,6 +95,19 @@ def block_mask_for(cfg):
     return ((kb <= qb) & ((qb - kb < 4) | (kb < 4))).astype(np.uint8)
 
 
+def kv_split_room(q, k, v, o, lse, cfg):
+    """Workspace bytes the launch asks for beyond its 256-byte counter without a block mask: room for
+    the partial results of KV splits (or, for causal ALiBi at d = 128, the far-tile bound)."""
+    import ctypes as C
+
+    import odf_b200
+
+    p, _keep = odf_b200.fill_params(q, k, v, o, lse, causal=cfg["causal"], scale=1.0 / math.sqrt(cfg["D"]),
+                                    block_mask=None, mask_block=(128, 128), alibi=cfg["alibi"],
+                                    alibi_slopes_host=None, softcap=cfg["softcap"], workspace=None, visits=None)
+    return odf_b200.load_library().odf_fwd_workspace_size(C.byref(p)) - 256
+
+
 def unmasked_pairs(cfg):
     """#unmasked (query, key) pairs of one (batch, q-head)."""
     return flop_per_unit_pairs(cfg) // (4 * cfg["D"])
@@ -99,11 +120,15 @@ def bias_planes(cfg):
 
 
 def flop_per_unit_pairs(cfg):
-    """Mask-adjusted FLOP of one (batch, q-head): 4 * d * #unmasked pairs."""
+    """Mask-adjusted FLOP of one (batch, q-head): 4 * d * #unmasked pairs (M query rows, default N)."""
     N, D = cfg["N"], cfg["D"]
+    M = cfg.get("M", N)
     mask = block_mask_for(cfg)
     if mask is None:
-        pairs = N * (N + 1) // 2 if cfg["causal"] else N * N
+        if cfg["causal"]:  # top-left: row qi sees keys 0..min(qi, N - 1)
+            pairs = M * (M + 1) // 2 if M <= N else N * (N + 1) // 2 + (M - N) * N
+        else:
+            pairs = M * N
     else:
         # element-level: allowed block and (causal) kj <= qi
         pairs = 0
@@ -348,7 +373,7 @@ def cpu_reference_sample(cfg, rows, steps, warmup, use_ref=True):
     if cfg.get("bias"):  # the reference's ScoreBiasFn path reads the same values
         shape = (1, 1, R, R) if cfg["bias"] == "broadcast" else (B, Hq, R, R)
         kw["bias"] = rng.standard_normal(shape).astype(np.float32)
-    sub = dict(cfg, N=R, mask=None)
+    sub = dict(cfg, N=R, M=R, mask=None)
     flop = flop_per_unit_pairs(sub) * B * Hq
     times = []
     for i in range(warmup + steps):
@@ -414,7 +439,7 @@ def batched_single_thread_sample(cfg, rows):
     q = oracle.round_bf16(rng.standard_normal((1, Hkv, R, D)).astype(np.float32) * cfg["in_scale"])
     k = oracle.round_bf16(rng.standard_normal((1, Hkv, R, D)).astype(np.float32) * cfg["in_scale"])
     v = oracle.round_bf16(rng.standard_normal((1, Hkv, R, D)).astype(np.float32) * cfg["in_scale"])
-    sub = dict(cfg, N=R, mask=None)
+    sub = dict(cfg, N=R, M=R, mask=None)
     flop = flop_per_unit_pairs(sub) * Hkv
     t0 = time.perf_counter()
     oracle.ref_fwd("batched", q, k, v, causal=cfg["causal"], q_block=16, k_block=32)
@@ -478,24 +503,29 @@ def run_ours(args, cfg, workload):
 
     cfg, seed = shard_config(cfg, rank, world, args.scaling)
     B, Hq, Hkv, N, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["N"], cfg["D"]
+    M = cfg.get("M", N)  # query rows
     out_dtype = torch.bfloat16 if cfg["out"] == "bf16" else torch.float32
     g = torch.Generator(device=dev).manual_seed(seed)
     s = cfg["in_scale"]
-    q = (torch.randn((B, Hq, N, D), generator=g, device=dev) * s).to(torch.bfloat16)
+    q = (torch.randn((B, Hq, M, D), generator=g, device=dev) * s).to(torch.bfloat16)
     k = (torch.randn((B, Hkv, N, D), generator=g, device=dev) * s).to(torch.bfloat16)
     v = (torch.randn((B, Hkv, N, D), generator=g, device=dev) * s).to(torch.bfloat16)
-    o = torch.empty((B, Hq, N, D), dtype=out_dtype, device=dev)
-    lse = torch.empty((B, Hq, N), dtype=torch.float32, device=dev)
+    o = torch.empty((B, Hq, M, D), dtype=out_dtype, device=dev)
+    lse = torch.empty((B, Hq, M), dtype=torch.float32, device=dev)
     mask = block_mask_for(cfg)
     bias = None
     if cfg.get("bias"):
-        bshape = (1, 1, N, N) if cfg["bias"] == "broadcast" else (B, Hq, N, N)
+        bshape = (1, 1, M, N) if cfg["bias"] == "broadcast" else (B, Hq, M, N)
         bias = torch.randn(bshape, generator=g, device=dev)
     flop_rank = flop_per_unit_pairs(cfg) * B * Hq
     # the library's own kernels per step: the block-mask tile lists, or for causal ALiBi at d = 128
     # the tile norms and the far-tile bound, then the forward kernel
     far_bound = cfg["alibi"] and cfg["causal"] and D == 128 and mask is None
     launches_per_step = 2 if mask is not None else (3 if far_bound else 1)
+    # launches that split their key range (workspace room beyond the 256-byte counter, no block
+    # mask, no far-tile bound) add the merge kernel
+    kv_splits = mask is None and not far_bound and kv_split_room(q, k, v, o, lse, cfg) > 0
+    launches_per_step += 1 if kv_splits else 0
 
     stream = torch.cuda.current_stream(dev)
 
@@ -505,7 +535,7 @@ def run_ours(args, cfg, workload):
 
     # algorithmic bytes: Q, K, V read once, O and LSE written once
     out_es = 2 if out_dtype == torch.bfloat16 else 4
-    alg_bytes = (B * Hq * N * D * 2 + 2 * B * Hkv * N * D * 2 + B * Hq * N * D * out_es + B * Hq * N * 4)
+    alg_bytes = (B * Hq * M * D * 2 + 2 * B * Hkv * N * D * 2 + B * Hq * M * D * out_es + B * Hq * M * 4)
     alg_bytes += unmasked_pairs(cfg) * 4 * bias_planes(cfg)  # the bias values the mask keeps, read once
     # Working sets under twice the 126 MB L2 get an L2 flush (a 256 MB write) between timed steps;
     # the value then sums the per-step event times, which exclude the flushes.
@@ -612,7 +642,8 @@ def run_ours(args, cfg, workload):
         roof = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                 "peak_kind": f"{peak_kind} HBM copy bandwidth", "tflops": achieved}
     roof.update({"traffic": profiled_traffic(args.config, args.seq_len), "algorithmic_bytes": alg_bytes,
-                 "kernel": f"flash_fwd_kernel<{D},{mod}>", "avg_launch_ms": avg_launch_ms})
+                 "kernel": f"flash_fwd_kernel<{D},{mod}>" + (" + split_combine_kernel" if kv_splits else ""),
+                 "avg_launch_ms": avg_launch_ms})
     if visited is not None:
         # causal ALiBi: far tiles (every score 48 (log2) below the row max by the norm bound) are
         # left out, so the tensor pipe runs only on the visited share of the algorithmic FLOP
@@ -639,7 +670,8 @@ def run_ours(args, cfg, workload):
             "config": {
                 "workload": workload,
                 "batch_per_gpu": B, "global_batch": B * world if args.scaling == "weak" else CONFIGS[args.config]["B"],
-                "heads_q_per_gpu": Hq, "heads_kv_per_gpu": Hkv, "seq_len": N,
+                "heads_q_per_gpu": Hq, "heads_kv_per_gpu": Hkv, "seq_len": N, "query_rows": M,
+                "kv_splits": bool(kv_splits),
                 "head_dim": D, "causal": cfg["causal"], "alibi": cfg["alibi"], "softcap": cfg["softcap"],
                 "block_mask": cfg["mask"], "bias": cfg.get("bias"), "out_dtype": cfg["out"], "lse": True,
                 "parallelism": f"(batch x head) shards, {world} GPU(s), no collective on the data path",
