@@ -1550,31 +1550,43 @@ __global__ void __launch_bounds__(256) split_combine_kernel(const float* __restr
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;  // whole warps leave together
+    // the splits' LSEs, lane l holding splits l, l + 32, ...: the row's max, then its weight sum
     float mx = -INFINITY;
-    for (int sp = 0; sp < n_splits; ++sp) mx = fmaxf(mx, __ldg(pl + sp * l_split + row));
+    for (int sp = lane; sp < n_splits; sp += 32) mx = fmaxf(mx, __ldg(pl + sp * l_split + row));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     float acc[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) acc[v] = 0.0f;
     float sum = 0.0f;
     if (mx != -INFINITY) {
-        for (int sp = 0; sp < n_splits; ++sp) {
-            const float l = __ldg(pl + sp * l_split + row);
-            if (l == -INFINITY) continue;
-            const float w = expf(l - mx);
-            sum += w;
-            const float* src = po + sp * o_split + row * D + lane * V;
-            if constexpr (V == 4) {
-                const float4 x = __ldg(reinterpret_cast<const float4*>(src));
-                acc[0] = fmaf(w, x.x, acc[0]);
-                acc[1] = fmaf(w, x.y, acc[1]);
-                acc[2] = fmaf(w, x.z, acc[2]);
-                acc[3] = fmaf(w, x.w, acc[3]);
-            } else {
-                const float2 x = __ldg(reinterpret_cast<const float2*>(src));
-                acc[0] = fmaf(w, x.x, acc[0]);
-                acc[1] = fmaf(w, x.y, acc[1]);
+        for (int base = 0; base < n_splits; base += 32) {
+            const int sp_l = base + lane;
+            const float l = sp_l < n_splits ? __ldg(pl + sp_l * l_split + row) : -INFINITY;
+            const float w_l = l == -INFINITY ? 0.0f : expf(l - mx);
+            sum += w_l;
+            const int cnt = min(32, n_splits - base);
+            // split t's O row, its weight broadcast from lane t; the loads are independent, so
+            // several are in flight at once
+#pragma unroll 8
+            for (int t = 0; t < cnt; ++t) {
+                const float w = __shfl_sync(0xffffffffu, w_l, t);
+                const float* src = po + (base + t) * o_split + row * D + lane * V;
+                if constexpr (V == 4) {
+                    const float4 x = __ldg(reinterpret_cast<const float4*>(src));
+                    acc[0] = fmaf(w, x.x, acc[0]);
+                    acc[1] = fmaf(w, x.y, acc[1]);
+                    acc[2] = fmaf(w, x.z, acc[2]);
+                    acc[3] = fmaf(w, x.w, acc[3]);
+                } else {
+                    const float2 x = __ldg(reinterpret_cast<const float2*>(src));
+                    acc[0] = fmaf(w, x.x, acc[0]);
+                    acc[1] = fmaf(w, x.y, acc[1]);
+                }
             }
         }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
     }
     const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
     const int64_t bh = row / m;
