@@ -85,6 +85,10 @@ def main():
                                      bias=rng.standard_normal((1, 4, 300, 500)).astype(np.float32))),
         ("host_pieces_alibi", dict(B=1, Hq=16, Hkv=2, M=1024, N=1024, D=128, causal=True, alibi=True, entry="host")),
         ("host_chunks_dense", dict(B=2, Hq=8, Hkv=8, M=384, N=512, D=128, entry="host")),
+        # KV splits: few items over long key ranges (split items, partial planes, merge)
+        ("kv_splits_decode_gqa", dict(B=1, Hq=4, Hkv=1, M=100, N=3000, D=128)),
+        ("kv_splits_causal_d64_softcap", dict(B=1, Hq=2, Hkv=2, M=256, N=2048, D=64, causal=True, softcap=20.0)),
+        ("kv_splits_host", dict(B=1, Hq=4, Hkv=2, M=100, N=3000, D=128, entry="host")),
     ]
     for name, kw in cases:
         print(json.dumps(run_case(name, **kw)), flush=True)

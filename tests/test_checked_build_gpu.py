@@ -1,6 +1,7 @@
 """The checked build (the library compiled with -DODF_CHECKED: in-kernel invariants on work-item
 decode, KV entries, the tensor-memory base, ring loads issued vs waited, P.V counts vs softmax
-tiles and the causal ALiBi bound) over problems that reach every scheduling and score-mod path:
+tiles and the causal ALiBi bound) over problems that reach every scheduling and score-mod path
+(KV splits included):
 no invariant may fail, the status word stays clean, and the results match the oracle.  The
 checked library runs in its own process (tests/checked_build_run.py)."""
 from __future__ import annotations
@@ -25,7 +26,7 @@ def test_checked_build_invariants_hold():
                           text=True, timeout=600, env=dict(os.environ))
     assert proc.returncode == 0, proc.stderr[-3000:]
     results = [json.loads(line) for line in proc.stdout.splitlines() if line.startswith("{")]
-    assert len(results) == 9, proc.stdout[-2000:]
+    assert len(results) == 12, proc.stdout[-2000:]
     for r in results:
         assert r["rc"] == 0 and r["check_bits"] == 0 and r["status"] == 0, r
         assert r["o_rel_l2"] <= 1e-2 and r["o_max_abs"] <= 2e-2 and r["lse_max_abs"] <= 1e-3, r

@@ -865,3 +865,34 @@ def test_kv_splits_host_entry_equals_device_entry(in_dtype):
     assert np.array_equal(lse, lse_dev)
     o_ref, lse_ref = oracle_fwd(q, k, v)
     check_close(o, lse, o_ref, lse_ref, "kv splits host entry")
+
+
+def test_kv_splits_fewer_when_workspace_is_smaller():
+    """A workspace with room for fewer splits than the plan asks for: the launch splits as many ways
+    as fit (here 3 instead of 6) and still matches the oracle."""
+    import ctypes as C
+
+    import odf_b200
+
+    torch = _torch()
+    B, H, Hk, M, N, D = 1, 2, 1, 64, 3000, 128
+    q, k, v = make_qkv(49, B, H, Hk, M, N, D)
+    up = lambda n: -(-n // 256) * 256
+    full = _splits_of(q, k, v)
+    assert full == up(6 * B * H * M * D * 4) + up(6 * B * H * M * 4)  # six splits of four KV tiles
+    room = up(3 * B * H * M * D * 4) + up(3 * B * H * M * 4)
+    qd, kd, vd = to_dev(q), to_dev(k), to_dev(v)
+    o = torch.empty((B, H, M, D), dtype=torch.float32, device="cuda")
+    lse = torch.empty((B, H, M), dtype=torch.float32, device="cuda")
+    ws = torch.zeros(256 + room, dtype=torch.uint8, device="cuda")
+    p, keep = odf_b200.fill_params(qd, kd, vd, o, lse, causal=False, scale=1.0 / math.sqrt(D), block_mask=None,
+                                   mask_block=(128, 128), alibi=False, alibi_slopes_host=None, softcap=0.0,
+                                   workspace=None, visits=None)
+    p.workspace = ws.data_ptr()
+    p.workspace_bytes = 256 + room
+    lib = odf_b200.load_library()
+    assert lib.odf_flash_fwd_sm100(C.byref(p), C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0, \
+        odf_b200.last_error()
+    torch.cuda.synchronize()
+    o_ref, lse_ref = oracle_fwd(q, k, v)
+    check_close(o.cpu().numpy(), lse.cpu().numpy(), o_ref, lse_ref, "kv splits in a smaller workspace")
