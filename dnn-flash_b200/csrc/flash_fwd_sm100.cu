@@ -853,30 +853,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::tmem_ld128(s_addr, s);
                 if constexpr ((MOD & kModSkipMax) != 0 && !Cfg::kSepP) {
                     // Unmasked tile, every row with a running max: the exponentials are taken against
-                    // that max straight away and the largest P is checked afterwards.  The max moves
-                    // only past 2^8; then S is read again and the general path below runs, so the
-                    // result is the same as with the max pass first.
+                    // that max straight away and the row's sum of P is checked afterwards.  The max
+                    // moves only past 2^8, which a sum of at most 2^8 rules out; otherwise S is read
+                    // again and the general path below runs (with the same P where the max stays), so
+                    // the result is the same as with the max pass first.
                     const bool interior = k0 + kTileK <= args.n && !(e & bitmap_bit) &&
                                           !(args.causal && k0 + kTileK - 1 > q0);
                     if (args.scale_log2 > 0.0f && interior && __all_sync(0xffffffffu, m_run != -INFINITY)) {
                         const uint64_t mul2 = ptx::f32x2(args.scale_log2);
                         const uint64_t neg2 = ptx::f32x2(-m_run);
                         uint64_t sum2[4] = {0, 0, 0, 0};
-                        float mx4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
                         for (int c = 0; c < 128; c += 2) {
                             const uint64_t x = ptx::ffma2(ptx::f32x2(s[c], s[c + 1]), mul2, neg2);
                             const float p0 = ptx::ex2(ptx::lo_f32(x));
                             const float p1 = ptx::ex2(ptx::hi_f32(x));
                             sum2[(c >> 1) & 3] = ptx::fadd2(sum2[(c >> 1) & 3], ptx::f32x2(p0, p1));
-                            mx4[(c >> 1) & 3] = ptx::fmax3(mx4[(c >> 1) & 3], p0, p1);
                             s[c >> 1] = __uint_as_float(ptx::pack_bf16x2(p0, p1));
                         }
-                        const float pmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-                        if (!__any_sync(0xffffffffu, pmax > 256.0f)) {
-                            const uint64_t sum4 =
-                                ptx::fadd2(ptx::fadd2(sum2[0], sum2[1]), ptx::fadd2(sum2[2], sum2[3]));
-                            l_run += ptx::lo_f32(sum4) + ptx::hi_f32(sum4);
+                        const uint64_t sum4 = ptx::fadd2(ptx::fadd2(sum2[0], sum2[1]), ptx::fadd2(sum2[2], sum2[3]));
+                        const float tile_sum = ptx::lo_f32(sum4) + ptx::hi_f32(sum4);
+                        // every P is positive, so a row sum of at most 2^8 bounds each P by 2^8 (no
+                        // separate max needed); a larger sum (rare) takes the exact path below
+                        if (!__any_sync(0xffffffffu, !(tile_sum <= 256.0f))) {
+                            l_run += tile_sum;
                             ptx::tmem_st64_nowait(p_addr, reinterpret_cast<const uint32_t*>(s));
                             ptx::tmem_st_wait();
                             ptx::tc_fence_before();
@@ -889,7 +889,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                             continue;
                         }
-                        ptx::tmem_ld128(s_addr, s);  // a row's max moved: the general path, from S again
+                        ptx::tmem_ld128(s_addr, s);  // a row's sum passed 2^8: the general path, from S again
                     }
                 }
                 if (Cfg::kSepP) {  // S_i is in registers: the next S_i may be computed now
