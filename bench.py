@@ -631,7 +631,7 @@ def run_ours(args, cfg, workload):
     avg_launch_ms = statistics.mean(per_launch_ms)
     achieved = flop_rank / (avg_launch_ms * 1e-3) / 1e12
     mod = (1 if cfg["alibi"] else 0) | (2 if cfg["softcap"] > 0 else 0) | (4 if cfg.get("bias") else 0)
-    if mod == 0 and D == 128 and cfg["mask"] is None and -(-N // 128) >= 48:
+    if mod == 0 and D == 128 and cfg["mask"] is None and -(-N // 128) >= 16:
         mod = 8  # the library's launch picks the variant that skips the row-max pass (kModSkipMax)
     if flop_rank / alg_bytes >= peak * 1e12 / (hbm * 1e9):  # above the ridge point: tensor-bound
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,

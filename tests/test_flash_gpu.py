@@ -596,12 +596,12 @@ def test_host_entry_matches_device_entry(in_dtype):
     check_close(o, lse, o_ref, lse_ref, "host entry")
 
 
-@pytest.mark.parametrize("spike_tile", [1, 30, 47])
-def test_running_max_jump_on_long_key_range(spike_tile):
-    """48 KV tiles (the variant that takes the exponentials against the running max before
+@pytest.mark.parametrize("n_tiles,spike_tile", [(48, 1), (48, 30), (48, 47), (16, 9), (16, 15)])
+def test_running_max_jump_on_long_key_range(n_tiles, spike_tile):
+    """16 or more KV tiles (the variant that takes the exponentials against the running max before
     checking it): one K tile scaled by 8 lifts its scores far above the running max, so rows whose
     max moves past 2^8 are recomputed with the max pass; O and LSE still match the oracle."""
-    q, k, v = make_qkv(51 + spike_tile, 1, 2, 2, 256, 48 * 128, 128)
+    q, k, v = make_qkv(51 + spike_tile + n_tiles, 1, 2, 2, 256, n_tiles * 128, 128)
     k[:, :, spike_tile * 128:(spike_tile + 1) * 128, :] *= 8.0  # a power of two: still bf16 values
     o, lse = run_gpu(q, k, v)
     o_ref, lse_ref = oracle_fwd(q, k, v)
